@@ -1,0 +1,438 @@
+"""bench.py — MoE-layer throughput of the B200 W4A8 library (driver contract).
+
+Workload (the metric's config): one Qwen3.6-35B-A3B-shaped MoE layer at
+decode — 32 tokens, hidden 2048, 256 routed experts (top-8 softmax routing from N(0,1)
+router logits, renormalised) plus 1 shared expert, gate_up K=2048 -> 2x512, SiLU-and-mul,
+down K=512 -> 2048, AWQ int4 g128 weights (codes U{0..15}, scales U[1e-3,2e-2], zeros
+U{0..15}), fp16 activations N(0,1). The shared expert rides the same grouped kernels as
+expert 256 with routing weight 1.0 on every token. `--workload prefill` runs configs[2]
+(4096 tokens, Zipf-biased routing).
+
+A step = one full layer forward (moe_align -> gate_up+SiLU -> down -> topk-weighted reduce)
+replayed from a CUDA graph with the inputs resident in HBM. Routing (softmax/top-k) is
+computed once outside the timed region. The touched expert weights (~270 MB at decode,
+~420 MB at prefill) exceed the 126 MB L2, so no explicit flush is needed.
+
+With --gpus N (torchrun, one rank per GPU) the layer runs expert-parallel: rank r owns experts
+[r*256/N, (r+1)*256/N) and its own 32 (decode) tokens; tokens reach the owners through NCCL
+all-to-all dispatch and come back through an all-to-all combine ("scaling": "weak").
+
+`--impl reference` times the reference's CPU implementation of the path (the numpy
+restatement of its torch oracle in oracle/w4a8_oracle.py) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "rdna4-vllm_b200"))
+sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+
+H, INTER, E_ROUTED, TOP_K, GROUP = 2048, 512, 256, 8, 128
+EXPERT_BYTES = (2 * INTER * H // 2 + 2 * INTER * (H // GROUP) * 2 + (2 * INTER // 8) * (H // GROUP) * 4
+                + H * INTER // 2 + H * (INTER // GROUP) * 2 + (H // 8) * (INTER // GROUP) * 4)
+W13_BYTES = 2 * INTER * H // 2 + 2 * INTER * (H // GROUP) * 2 + (2 * INTER // 8) * (H // GROUP) * 4
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], 2 * d["bf16_tflops"], "measured"
+    return 6650.0, 2 * 1590.0, "fallback"
+
+
+def workload_config(name: str):
+    if name == "prefill":
+        return dict(T=4096, zipf=True, seed=2)
+    return dict(T=32, zipf=False, seed=1)
+
+
+# ------------------------------------------------------------------------------------------
+# clocks sampling (nvidia-smi during the timed region)
+# ------------------------------------------------------------------------------------------
+class ClockSampler:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"w4a8_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait(timeout=5)
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [v.strip() for v in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------
+# synthetic layer
+# ------------------------------------------------------------------------------------------
+def make_layer(torch, dev, seed: int, E: int):
+    """Per-expert AWQ-style weights generated on the device (uniform nibbles == uniform words)."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    def words(*shape):
+        return torch.randint(-2 ** 31, 2 ** 31 - 1, shape, dtype=torch.int32, device=dev, generator=g)
+    def scales(*shape):
+        return (torch.rand(shape, device=dev, generator=g) * (2e-2 - 1e-3) + 1e-3).to(torch.float16)
+    w13 = words(E, 2 * INTER, H // 8)
+    s13 = scales(E, 2 * INTER, H // GROUP)
+    z13 = words(E, 2 * INTER // 8, H // GROUP)
+    w2 = words(E, H, INTER // 8)
+    s2 = scales(E, H, INTER // GROUP)
+    z2 = words(E, H // 8, INTER // GROUP)
+    return w13, s13, z13, w2, s2, z2
+
+
+def make_tokens(T: int, zipf: bool, seed: int):
+    """Host-side seeded tokens and routing; the shared expert is slot TOP_K (id 256, w 1.0)."""
+    import inputs as I
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((T, H), dtype=np.float32).astype(np.float16)
+    _, ids, w = I.routing(rng, T, E_ROUTED, TOP_K, zipf_bias=zipf)
+    ids = np.concatenate([ids, np.full((T, 1), E_ROUTED, np.int32)], axis=1)
+    w = np.concatenate([w, np.ones((T, 1), np.float32)], axis=1)
+    return x, ids.astype(np.int32), w.astype(np.float32)
+
+
+# ------------------------------------------------------------------------------------------
+# the B200 arm
+# ------------------------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import w4a8_fp8_wmma as w4
+    from w4a8_fp8_wmma.moe_experts import run_grouped_moe
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    cfg = workload_config(args.workload)
+    T = cfg["T"]
+    E_total = E_ROUTED + 1
+    if world > 1:
+        from w4a8_fp8_wmma.ep import ExpertParallelMoE
+        layer = ExpertParallelMoE.synthetic(E_ROUTED, H, INTER, GROUP, TOP_K, seed=1000, dev=dev)
+        x_np, ids_np, w_np = make_tokens(T, cfg["zipf"], cfg["seed"] * 1000 + rank)
+        step_fn, out_holder, inputs = layer.make_step(x_np, ids_np[:, :TOP_K], w_np[:, :TOP_K], T)
+        touched_bytes = layer.local_bytes()
+    else:
+        w13, s13, z13, w2, s2, z2 = make_layer(torch, dev, 1000, E_total)
+        x_np, ids_np, w_np = make_tokens(T, cfg["zipf"], cfg["seed"])
+        x = torch.from_numpy(x_np).to(dev)
+        ids = torch.from_numpy(ids_np).to(dev)
+        tw = torch.from_numpy(w_np).to(dev)
+        touched = np.unique(ids_np)
+        touched_bytes = len(touched) * EXPERT_BYTES
+        out_holder = {}
+
+        def step_fn():
+            out_holder["y"] = run_grouped_moe(x, w13, w2, s13, s2, z13, z2, tw, ids,
+                                              global_num_experts=E_total, out_dtype=torch.float16)
+
+    # CUDA graph of one step.
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            step_fn()
+    torch.cuda.current_stream().wait_stream(stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step_fn()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    tokens_per_s = T * world / (ms / 1e3)
+
+    # Dominant kernel: time the gate_up grouped GEMM alone (same inputs) with CUDA events.
+    dom = dominant_kernel(torch, w4, args, world, layer if world > 1 else None,
+                          locals().get("x"), locals().get("ids"), locals().get("w13"),
+                          locals().get("s13"), locals().get("z13"), E_total, T)
+
+    # End to end through the public API: pinned host inputs -> device -> layer -> host output.
+    e2e = end_to_end(torch, args, world, locals())
+    hbm, fp8_peak, src = peaks()
+    layer_bytes = touched_bytes + T * H * 2 * 2 + T * (TOP_K + 1) * 8
+    flops = 2.0 * T * (TOP_K + 1) * (H * 2 * INTER + INTER * H)
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    res = {
+        "metric": "MoE-layer tokens/s (Qwen3.6-35B-A3B-shaped, decode T=32)"
+        if args.workload == "decode" else "MoE-layer tokens/s (Qwen3.6-35B-A3B-shaped, prefill T=4096)",
+        "value": round(tokens_per_s, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 x int4 -> fp32 (fp16 io)",
+        "data": "synthetic (seeded; random-init weights of the layer's shapes)",
+        "config": {"workload": f"configs[{1 if args.workload == 'decode' else 2}] MoE layer {args.workload}",
+                   "tokens_per_gpu": T, "hidden": H, "inter": INTER, "experts": E_ROUTED,
+                   "shared_experts": 1, "top_k": TOP_K, "group": GROUP,
+                   "parallelism": f"ep{world}" if world > 1 else "single",
+                   "l2": "touched weights > 126 MB L2 (no flush)",
+                   "layer_hbm_gbs": round(layer_bytes / (ms / 1e3) / 1e9, 1),
+                   "layer_hbm_frac_of_measured": round(layer_bytes / (ms / 1e3) / 1e9 / hbm, 4),
+                   "layer_tflops": round(flops / (ms / 1e3) / 1e12, 2),
+                   "graph": "one CUDA graph per step"},
+        "roofline": dom,
+        "clocks": clk.summary(),
+        "e2e": e2e,
+        "gpu_launches": args.steps * launches_per_step(args.workload, world),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline(args.workload, budget_s=args.cpu_seconds)
+    print(json.dumps(res))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def launches_per_step(workload: str, world: int) -> int:
+    # align (2) + act-quant + gate_up/SiLU + act-quant + down + [gather-reduce: memset-free map
+    # build + reduce at prefill]
+    n = 6 if workload == "decode" else 8
+    if world > 1:
+        n += 4  # dispatch pack / unpack, combine pack / unpack
+    return n
+
+
+def dominant_kernel(torch, w4, args, world, layer, x, ids, w13, s13, z13, E_total, T):
+    hbm, _, src = peaks()
+    if world > 1:
+        return layer.dominant_kernel_roofline(hbm, src)
+    block_m = 8 if T <= 96 else 64
+    kern = 7 if T <= 96 else 6
+    s, e, n = w4.moe_align_block_size(ids, block_m, E_total)
+    zero = torch.empty(0, dtype=torch.int32, device=x.device)
+    def launch():
+        return torch.ops.w4a8_b200.moe_gemm1_silu(x, w13, s13, z13, s, e, n, ids.size(1), block_m,
+                                                  kern, False)
+    for _ in range(3):
+        launch()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 20
+    a.record(st)
+    for _ in range(reps):
+        launch()
+    b.record(st)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / reps  # includes the act-quant launch of x (tiny)
+    touched = torch.unique(ids).numel()
+    bytes_ = touched * W13_BYTES + T * H + T * 4 + int(n.item()) * INTER * 2
+    ach = bytes_ / (ms / 1e3) / 1e9
+    return {"kernel": "w4_mma_kernel<gate_up+SiLU> (+act_quant)", "bound": "hbm",
+            "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s", "frac": round(ach / hbm, 4),
+            "peak_source": src, "algorithmic_bytes_per_launch": bytes_,
+            "avg_launch_us": round(ms * 1e3, 2), "traffic": None}
+
+
+def end_to_end(torch, args, world, env):
+    """Same metric through the public API with host buffers (pinned), copies inside timing."""
+    from w4a8_fp8_wmma.moe_experts import run_grouped_moe
+    if world > 1:
+        return env["layer"].end_to_end(args.steps, env["x_np"], env["ids_np"], env["w_np"])
+    x_h = torch.from_numpy(env["x_np"]).pin_memory()
+    ids_h = torch.from_numpy(env["ids_np"]).pin_memory()
+    w_h = torch.from_numpy(env["w_np"]).pin_memory()
+    dev = env["x"].device
+    w13, w2, s13, s2, z13, z2 = (env[k] for k in ("w13", "w2", "s13", "s2", "z13", "z2"))
+    out_h = torch.empty((env["T"], H), dtype=torch.float16).pin_memory()
+    def once():
+        x = x_h.to(dev, non_blocking=True)
+        ids = ids_h.to(dev, non_blocking=True)
+        tw = w_h.to(dev, non_blocking=True)
+        y = run_grouped_moe(x, w13, w2, s13, s2, z13, z2, tw, ids,
+                            global_num_experts=env["E_total"], out_dtype=torch.float16)
+        out_h.copy_(y, non_blocking=True)
+    for _ in range(3):
+        once()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(st)
+    for _ in range(args.steps):
+        once()
+    b.record(st)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    T = env["T"]
+    return {"value": round(T / (ms / 1e3), 1), "unit": "tokens/s",
+            "h2d_bytes_per_step": int(x_h.numel() * 2 + ids_h.numel() * 4 + w_h.numel() * 4),
+            "d2h_bytes_per_step": int(out_h.numel() * 2), "ms_per_step": round(ms, 4),
+            "path": "w4a8_fp8_wmma.moe_experts.run_grouped_moe (eager, no graph)"}
+
+
+# ------------------------------------------------------------------------------------------
+# CPU baseline / reference arm: the reference's CPU algorithm (numpy oracle port)
+# ------------------------------------------------------------------------------------------
+def cpu_layer_sample(workload: str, budget_s: float):
+    """Time the oracle MoE layer on a bounded sample; returns (tokens/s, sample text)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import w4a8_oracle as O
+    cfg = workload_config(workload)
+    T = cfg["T"]
+    x, ids, w = make_tokens(T, cfg["zipf"], cfg["seed"])
+    rng = np.random.default_rng(5)
+    used = np.unique(ids)
+    # Only the experts the sample touches are materialised (host memory stays small).
+    def rand_w(n, k):
+        return rng.integers(-2 ** 31, 2 ** 31 - 1, (n, k), dtype=np.int64).astype(np.int32)
+    E_total = E_ROUTED + 1
+    w13 = np.zeros((E_total, 2 * INTER, H // 8), np.int32)
+    w2 = np.zeros((E_total, H, INTER // 8), np.int32)
+    s13 = np.zeros((E_total, 2 * INTER, H // GROUP), np.float16)
+    s2 = np.zeros((E_total, H, INTER // GROUP), np.float16)
+    z13 = np.zeros((E_total, 2 * INTER // 8, H // GROUP), np.int32)
+    z2 = np.zeros((E_total, H // 8, INTER // GROUP), np.int32)
+    for e in used:
+        w13[e] = rand_w(2 * INTER, H // 8)
+        w2[e] = rand_w(H, INTER // 8)
+        s13[e] = rng.uniform(1e-3, 2e-2, (2 * INTER, H // GROUP))
+        s2[e] = rng.uniform(1e-3, 2e-2, (H, INTER // GROUP))
+        z13[e] = rand_w(2 * INTER // 8, H // GROUP)
+        z2[e] = rand_w(H // 8, INTER // GROUP)
+    # Bounded sample: a prefix of the tokens, grown until ~budget_s of CPU work.
+    n = min(T, 32)
+    t0 = time.perf_counter()
+    O.moe_layer(x[:n], w13, s13, z13, w2, s2, z2, ids[:n], w[:n])
+    dt = time.perf_counter() - t0
+    reps = max(1, int(budget_s / max(dt, 1e-3)))
+    reps = min(reps, 20)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        O.moe_layer(x[:n], w13, s13, z13, w2, s2, z2, ids[:n], w[:n])
+    dt = (time.perf_counter() - t0) / reps
+    return n / dt, f"{n} of {T} tokens of the {workload} layer (top-8 + shared), {reps} timed reps"
+
+
+def cpu_baseline(workload: str, budget_s: float = 10.0):
+    v, sample = cpu_layer_sample(workload, budget_s)
+    return {"value": round(v, 2), "unit": "tokens/s", "cores": _threads(), "kind": "port",
+            "sample": sample}
+
+
+def _threads() -> int:
+    try:
+        import threadpoolctl
+        info = threadpoolctl.threadpool_info()
+        return int(max((i.get("num_threads", 1) for i in info), default=1))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    for _ in range(args.warmup):
+        cpu_layer_sample(args.workload, 0.0)
+    vals = []
+    for _ in range(args.steps):
+        v, sample = cpu_layer_sample(args.workload, 0.0)
+        vals.append(v)
+    v = float(np.median(vals))
+    cfg = workload_config(args.workload)
+    res = {
+        "impl": "reference",
+        "metric": "MoE-layer tokens/s (Qwen3.6-35B-A3B-shaped, decode T=32)"
+        if args.workload == "decode" else "MoE-layer tokens/s (Qwen3.6-35B-A3B-shaped, prefill T=4096)",
+        "value": round(v, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "e4m3 x int4 -> fp32 (fp16 io)", "data": "synthetic (seeded)",
+        "config": {"workload": f"configs[{1 if args.workload == 'decode' else 2}] MoE layer {args.workload}",
+                   "tokens_per_gpu": cfg["T"]},
+        "cpu_baseline": {"value": round(v, 2), "unit": "tokens/s", "cores": _threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(v, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "reference HIP kernels target gfx1201 only; its CPU algorithm (torch oracle) is "
+                "restated in numpy (oracle/w4a8_oracle.py) and timed on the host cores",
+    }
+    print(json.dumps(res))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

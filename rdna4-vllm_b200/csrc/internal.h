@@ -1,0 +1,13 @@
+// internal.h — launchers shared between the translation units of libw4a8_b200.so.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace w4a8 {
+
+int launch_act_quant(const void* x, uint8_t* xq, float* scales, int64_t M, int64_t K,
+                     cudaStream_t stream);
+
+}  // namespace w4a8

@@ -1,0 +1,168 @@
+// moe_align.cu — deterministic moe_align_block_size.
+//
+// Order contract (the reference's Python moe_align, w4a8_fp8_wmma/test_moe_correctness.py:49-67):
+// experts ascending; inside an expert, slot ids (t*top_k + j) ascending; each expert's run is
+// padded up to a multiple of block_m with the sentinel num_slots; an expert with no slots gets
+// no block; num_tokens_post_padded = total padded length.
+//
+// Two launches:
+//   1. align_count_kernel (one CTA): per-expert histogram in shared memory, exclusive scan of
+//      the padded counts into `offsets` (workspace), expert_ids per block, the tail fill.
+//   2. align_place_kernel (one warp per local expert): each warp walks the slot list in order
+//      with __ballot_sync and writes its expert's slots at offsets[e] + running rank, which is
+//      stable by construction; then the warp writes its padding sentinels.
+// The slot list is staged in shared memory as int16 local expert ids when it fits.
+#include "common.cuh"
+#include "internal.h"
+
+namespace w4a8 {
+
+namespace {
+
+constexpr int kCountThreads = 1024;
+constexpr int kPlaceWarps = 8;
+constexpr int64_t kMaxSmemSlots = 96 * 1024 / 2;  // int16 ids in 96 KB of shared memory
+
+__device__ __forceinline__ int local_expert(const int32_t* __restrict__ topk_ids,
+                                            const int32_t* __restrict__ expert_map, int64_t i,
+                                            int num_experts) {
+    const int e = topk_ids[i];
+    if (e < 0 || e >= num_experts) return -1;
+    return expert_map ? expert_map[e] : e;
+}
+
+__global__ void __launch_bounds__(kCountThreads)
+align_count_kernel(const int32_t* __restrict__ topk_ids, int64_t num_slots, int num_experts,
+                   int num_local, int block_m, const int32_t* __restrict__ expert_map,
+                   int32_t* __restrict__ sorted_ids, int64_t capacity,
+                   int32_t* __restrict__ expert_ids, int32_t* __restrict__ ntp_out,
+                   int32_t* __restrict__ offsets) {
+    extern __shared__ int32_t counts[];  // num_local entries
+    __shared__ int32_t partial[kCountThreads];
+    const int tid = threadIdx.x;
+    for (int e = tid; e < num_local; e += kCountThreads) counts[e] = 0;
+    __syncthreads();
+    for (int64_t i = tid; i < num_slots; i += kCountThreads) {
+        const int le = local_expert(topk_ids, expert_map, i, num_experts);
+        if (le >= 0 && le < num_local) atomicAdd(&counts[le], 1);
+    }
+    __syncthreads();
+    // Contiguous chunk of experts per thread -> local padded sum -> block exclusive scan.
+    const int per = (num_local + kCountThreads - 1) / kCountThreads;
+    const int e0 = min(tid * per, num_local), e1 = min(e0 + per, num_local);
+    int32_t local = 0;
+    for (int e = e0; e < e1; ++e) local += (counts[e] + block_m - 1) / block_m * block_m;
+    partial[tid] = local;
+    __syncthreads();
+    for (int off = 1; off < kCountThreads; off <<= 1) {  // Hillis-Steele inclusive scan
+        const int32_t v = tid >= off ? partial[tid - off] : 0;
+        __syncthreads();
+        partial[tid] += v;
+        __syncthreads();
+    }
+    int32_t run = partial[tid] - local;  // exclusive prefix of this thread's chunk
+    for (int e = e0; e < e1; ++e) {
+        offsets[e] = run;
+        const int32_t padded = (counts[e] + block_m - 1) / block_m * block_m;
+        for (int32_t b = run / block_m; b < (run + padded) / block_m; ++b) expert_ids[b] = e;
+        run += padded;
+    }
+    const int32_t total = partial[kCountThreads - 1];
+    if (tid == 0) {
+        offsets[num_local] = total;
+        ntp_out[0] = total;
+    }
+    const int32_t sentinel = (int32_t)num_slots;
+    for (int64_t i = total + tid; i < capacity; i += kCountThreads) sorted_ids[i] = sentinel;
+    for (int64_t b = total / block_m + tid; b < capacity / block_m; b += kCountThreads)
+        expert_ids[b] = -1;
+}
+
+template <bool kSmem>
+__global__ void __launch_bounds__(kPlaceWarps * 32)
+align_place_kernel(const int32_t* __restrict__ topk_ids, int64_t num_slots, int num_experts,
+                   int num_local, const int32_t* __restrict__ expert_map,
+                   const int32_t* __restrict__ offsets, int32_t* __restrict__ sorted_ids) {
+    extern __shared__ int16_t ids[];
+    if (kSmem) {
+        for (int64_t i = threadIdx.x; i < num_slots; i += blockDim.x)
+            ids[i] = (int16_t)local_expert(topk_ids, expert_map, i, num_experts);
+        __syncthreads();
+    }
+    const int lane = threadIdx.x & 31;
+    const int e = blockIdx.x * kPlaceWarps + (threadIdx.x >> 5);
+    if (e >= num_local) return;
+    const int32_t base = offsets[e];
+    const int32_t end = offsets[e + 1];
+    const uint32_t lt = (1u << lane) - 1u;
+    int32_t run = base;
+    for (int64_t c = 0; c < num_slots; c += 32) {
+        const int64_t i = c + lane;
+        int le = -1;
+        if (i < num_slots) le = kSmem ? (int)ids[i] : local_expert(topk_ids, expert_map, i, num_experts);
+        const uint32_t m = __ballot_sync(0xffffffffu, le == e);
+        if (le == e) sorted_ids[run + __popc(m & lt)] = (int32_t)i;
+        run += __popc(m);
+    }
+    const int32_t sentinel = (int32_t)num_slots;
+    for (int32_t p = run + lane; p < end; p += 32) sorted_ids[p] = sentinel;
+}
+
+}  // namespace
+
+}  // namespace w4a8
+
+extern "C" size_t w4a8_moe_align_workspace_size(int32_t num_local_experts) {
+    return w4a8::align_up(((size_t)num_local_experts + 1) * sizeof(int32_t), 256);
+}
+
+extern "C" int w4a8_moe_align_block_size(const int32_t* topk_ids, int64_t num_slots,
+                                         int32_t num_experts, int32_t num_local_experts,
+                                         int32_t block_m, const int32_t* expert_map,
+                                         int32_t* sorted_token_ids, int64_t sorted_capacity,
+                                         int32_t* expert_ids, int32_t* num_tokens_post_padded,
+                                         void* workspace, size_t workspace_bytes,
+                                         w4a8_stream_t stream) {
+    using namespace w4a8;
+    if (num_slots < 0 || num_experts <= 0 || num_local_experts <= 0 || block_m <= 0)
+        return set_error("moe_align: sizes must be positive");
+    if (num_slots >= (int64_t)INT32_MAX) return set_error("moe_align: too many slots");
+    if (num_local_experts > 32767) return set_error("moe_align: at most 32767 local experts");
+    if (!expert_map && num_local_experts != num_experts)
+        return set_error("moe_align: num_local_experts must equal num_experts without a map");
+    if (sorted_capacity % block_m != 0)
+        return set_error("moe_align: sorted capacity must be a multiple of block_m");
+    const int64_t need = num_slots + (int64_t)num_local_experts * (block_m - 1);
+    if (sorted_capacity < need)
+        return set_error("moe_align: sorted capacity " + std::to_string(sorted_capacity) +
+                         " < num_slots + E*(block_m-1) = " + std::to_string(need));
+    if (!topk_ids || !sorted_token_ids || !expert_ids || !num_tokens_post_padded)
+        return set_error("moe_align: null pointer");
+    if (workspace_bytes < w4a8_moe_align_workspace_size(num_local_experts) || !workspace)
+        return set_error("moe_align: workspace too small");
+    int32_t* offsets = static_cast<int32_t*>(workspace);
+    const size_t count_smem = (size_t)num_local_experts * sizeof(int32_t);
+    if (count_smem > 48 * 1024) {
+        cudaFuncSetAttribute(align_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)count_smem);
+    }
+    align_count_kernel<<<1, kCountThreads, count_smem, stream>>>(
+        topk_ids, num_slots, num_experts, num_local_experts, block_m, expert_map,
+        sorted_token_ids, sorted_capacity, expert_ids, num_tokens_post_padded, offsets);
+    int st = launch_status();
+    if (st) return st;
+    const dim3 grid((num_local_experts + kPlaceWarps - 1) / kPlaceWarps);
+    if (num_slots <= kMaxSmemSlots) {
+        const size_t smem = align_up((size_t)num_slots * sizeof(int16_t), 16);
+        cudaFuncSetAttribute(align_place_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(kMaxSmemSlots * sizeof(int16_t)));
+        align_place_kernel<true><<<grid, kPlaceWarps * 32, smem, stream>>>(
+            topk_ids, num_slots, num_experts, num_local_experts, expert_map, offsets,
+            sorted_token_ids);
+    } else {
+        align_place_kernel<false><<<grid, kPlaceWarps * 32, 0, stream>>>(
+            topk_ids, num_slots, num_experts, num_local_experts, expert_map, offsets,
+            sorted_token_ids);
+    }
+    return launch_status();
+}

@@ -1,0 +1,87 @@
+// reduce.cu — topk-weighted gather-reduce of the down-projection rows back to tokens.
+//
+// Semantics of mmq_fp8_moe_gather_reduce (w4a8_fp8_wmma/moe_kernel.hip:1230-1262):
+//   slot_to_row[slot] = r for every r < ntp with sorted_token_ids[r] = slot < M*top_k, else -1;
+//   out[t, n] = sum_{j ascending} w[t*top_k + j] * out2[slot_to_row[t*top_k + j], n]   (fp32)
+// The sum is a plain fp32 multiply then add in slot order, the order the reference oracle uses
+// (w4a8_fp8_wmma/test_moe_experts.py:182-190).
+#include "common.cuh"
+#include "internal.h"
+
+namespace w4a8 {
+
+namespace {
+
+__global__ void build_inverse_map_kernel(const int32_t* __restrict__ sorted_ids,
+                                         const int32_t* __restrict__ ntp, int32_t* slot_to_row,
+                                         int64_t P, int64_t num_slots) {
+    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= P || r >= ntp[0]) return;
+    const int32_t slot = sorted_ids[r];
+    if (slot >= 0 && slot < num_slots) slot_to_row[slot] = (int32_t)r;
+}
+
+// One CTA per (token, 512-channel chunk); each thread reduces 2 adjacent channels.
+__global__ void __launch_bounds__(256)
+gather_reduce_kernel(const __half* __restrict__ out2, const int32_t* __restrict__ slot_to_row,
+                     const float* __restrict__ topk_w, float* __restrict__ out, int64_t N,
+                     int top_k) {
+    const int64_t t = blockIdx.y;
+    const int64_t n = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 2;
+    if (n >= N) return;
+    float a0 = 0.f, a1 = 0.f;
+    const bool pair = (n + 1 < N);
+    for (int j = 0; j < top_k; ++j) {
+        const int32_t r = slot_to_row[t * top_k + j];
+        if (r < 0) continue;
+        const float w = topk_w[t * top_k + j];
+        const __half* rowp = out2 + (int64_t)r * N + n;
+        if (pair && (N % 2 == 0)) {
+            const __half2 v = *reinterpret_cast<const __half2*>(rowp);
+            a0 = __fadd_rn(a0, __fmul_rn(w, __low2float(v)));
+            a1 = __fadd_rn(a1, __fmul_rn(w, __high2float(v)));
+        } else {
+            a0 = __fadd_rn(a0, __fmul_rn(w, __half2float(rowp[0])));
+            if (pair) a1 = __fadd_rn(a1, __fmul_rn(w, __half2float(rowp[1])));
+        }
+    }
+    out[t * N + n] = a0;
+    if (pair) out[t * N + n + 1] = a1;
+}
+
+}  // namespace
+
+}  // namespace w4a8
+
+extern "C" size_t w4a8_moe_gather_reduce_workspace_size(int64_t M, int64_t top_k) {
+    return w4a8::align_up((size_t)(M * top_k) * sizeof(int32_t), 256);
+}
+
+extern "C" int w4a8_moe_gather_reduce(const void* out2, const int32_t* sorted_token_ids,
+                                      const float* topk_weights,
+                                      const int32_t* num_tokens_post_padded, float* out,
+                                      int64_t M, int64_t N, int64_t P, int64_t top_k,
+                                      void* workspace, size_t workspace_bytes,
+                                      w4a8_stream_t stream) {
+    using namespace w4a8;
+    if (M < 0 || N <= 0 || P < 0 || top_k <= 0) return set_error("gather_reduce: bad sizes");
+    if (M * top_k > INT32_MAX) return set_error("gather_reduce: size overflow");
+    if (M == 0) return W4A8_OK;
+    if (!out || !topk_weights || (P > 0 && (!out2 || !sorted_token_ids || !num_tokens_post_padded)))
+        return set_error("gather_reduce: null pointer");
+    if (!workspace || workspace_bytes < w4a8_moe_gather_reduce_workspace_size(M, top_k))
+        return set_error("gather_reduce: workspace too small");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    int32_t* map = static_cast<int32_t*>(workspace);
+    cudaError_t e = cudaMemsetAsync(map, 0xFF, (size_t)(M * top_k) * sizeof(int32_t), st);
+    if (e != cudaSuccess) return (int)e;
+    if (P > 0) {
+        build_inverse_map_kernel<<<(unsigned)((P + 255) / 256), 256, 0, st>>>(
+            sorted_token_ids, num_tokens_post_padded, map, P, M * top_k);
+        if (int rc = launch_status()) return rc;
+    }
+    const dim3 grid((unsigned)((N + 511) / 512), (unsigned)M);
+    gather_reduce_kernel<<<grid, 256, 0, st>>>(static_cast<const __half*>(out2), map,
+                                               topk_weights, out, N, (int)top_k);
+    return launch_status();
+}

@@ -1,0 +1,156 @@
+"""Grouped-MoE composition and checkpoint-layout converters (vLLM-free).
+
+``run_grouped_moe`` mirrors the reference's ``_run_grouped_moe``
+(w4a8_fp8_wmma/w4a8_fp8_wmma/moe_experts.py:493-665): moe_align -> gate_up GEMM fused with
+silu_and_mul -> down GEMM -> topk-weighted reduce, with the same decode/prefill split
+(M <= 96 takes the GEMV kernels with block_m 8 and the atomic-scatter epilogue; larger M takes
+the tile kernels with block_m 64, a materialised down output and the gather-reduce) and the same
+4096-token chunking. Every step is one of this package's CUDA ops; the routing sort is this
+library's deterministic moe_align_block_size instead of vLLM's.
+
+Converters restate the reference's load-time layout changes:
+AWQ (moe_experts.py:331-396), compressed-tensors GPTQ (:409-454), MoeWNA16 (:473-482).
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+
+from . import (moe_align_block_size, mmq_fp8_moe_gather_reduce, mmq_fp8_moe_gemm,
+               mmq_fp8_moe_gemm_scatter)
+
+AWQ_REVERSE_PACK_ORDER = [0, 4, 1, 5, 2, 6, 3, 7]
+GEMV_MAX_M = int(os.environ.get("VLLM_ROCM_W4A8_FP8_WMMA_MOE_GEMV_MAX_M", "96"))
+GEMV_BLOCK_M = int(os.environ.get("VLLM_ROCM_W4A8_FP8_WMMA_MOE_GEMV_BLOCK_M", "8"))
+TILE_BLOCK_M = int(os.environ.get("VLLM_ROCM_W4A8_FP8_WMMA_MOE_BLOCK_M", "64"))
+APPLY_CHUNK = int(os.environ.get("VLLM_ROCM_W4A8_FP8_WMMA_MOE_APPLY_CHUNK", "4096"))
+
+_MOE_IDS = {"scalar": 0, "wmma": 6, "gemv": 7}
+
+
+def _gemm1_silu(x, w, s, z, sorted_ids, expert_ids, ntp, top_k, block_m, kernel):
+    if z is None:
+        z = torch.empty(0, dtype=torch.int32, device=x.device)
+    return torch.ops.w4a8_b200.moe_gemm1_silu(x, w, s, z, sorted_ids, expert_ids, ntp, top_k,
+                                              block_m, _MOE_IDS[kernel], False)
+
+
+def run_grouped_moe(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, w1_s: torch.Tensor,
+                    w2_s: torch.Tensor, w1_zp: torch.Tensor | None, w2_zp: torch.Tensor | None,
+                    topk_weights: torch.Tensor, topk_ids: torch.Tensor, kernel: str = "wmma",
+                    global_num_experts: int | None = None,
+                    expert_map: torch.Tensor | None = None,
+                    apply_router_weight_on_input: bool = False,
+                    out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """Whole gated MoE in the op layout; returns (M, K) already topk-weighted and reduced.
+
+    w1 (E, 2*inter, K/8) int32 [gate | up], w2 (E, K, inter/8) int32, scales (E, N, K/g) fp16,
+    zeros (E, N/8, K/g) int32 or None (symmetric zp 8). ``expert_map`` maps global expert ids
+    to local ones (-1 = remote); remote slots contribute nothing.
+    """
+    M, K = x.shape
+    top_k = topk_ids.size(1)
+    E_local = w1.size(0)
+    E_global = int(global_num_experts) if global_num_experts is not None else E_local
+    dev = x.device
+    out_dtype = out_dtype or x.dtype
+    if APPLY_CHUNK and M > APPLY_CHUNK and not apply_router_weight_on_input:
+        out = torch.empty((M, K), dtype=out_dtype, device=dev)
+        for lo in range(0, M, APPLY_CHUNK):
+            hi = min(lo + APPLY_CHUNK, M)
+            out[lo:hi] = run_grouped_moe(x[lo:hi], w1, w2, w1_s, w2_s, w1_zp, w2_zp,
+                                         topk_weights[lo:hi], topk_ids[lo:hi], kernel,
+                                         global_num_experts, expert_map, False, out_dtype)
+        return out
+    use_gemv = kernel != "scalar" and M <= GEMV_MAX_M
+    block_m = GEMV_BLOCK_M if use_gemv else TILE_BLOCK_M
+    gver = "gemv" if use_gemv else kernel
+    sorted_ids, expert_ids, ntp = moe_align_block_size(
+        topk_ids, block_m, E_global, expert_map, E_local)
+    x_in = x
+    if apply_router_weight_on_input:
+        assert top_k == 1, "router-weight-on-input requires top_k == 1"
+        x_in = x_in * topk_weights.reshape(M, 1).to(x_in.dtype)
+    x16 = x_in.to(torch.float16).contiguous()
+    w1_s = w1_s if w1_s.dtype == torch.float16 else w1_s.to(torch.float16)
+    w2_s = w2_s if w2_s.dtype == torch.float16 else w2_s.to(torch.float16)
+    buf2 = _gemm1_silu(x16, w1, w1_s, w1_zp, sorted_ids, expert_ids, ntp, top_k, block_m, gver)
+    if apply_router_weight_on_input:
+        tw = torch.ones(M * top_k, dtype=torch.float32, device=dev)
+    else:
+        tw = topk_weights.reshape(-1).to(torch.float32).contiguous()
+    if use_gemv:
+        output = torch.zeros((M, K), dtype=torch.float32, device=dev)
+        mmq_fp8_moe_gemm_scatter(buf2, w2, w2_s, sorted_ids, expert_ids, ntp, tw, output, top_k,
+                                 block_m, kernel=gver, w_zeros=w2_zp)
+        return output.to(out_dtype)
+    ident = torch.arange(sorted_ids.numel(), dtype=torch.int32, device=dev)
+    out2 = mmq_fp8_moe_gemm(buf2, w2, w2_s, ident, expert_ids, ntp, 1, block_m, kernel=kernel,
+                            w_zeros=w2_zp)
+    acc = mmq_fp8_moe_gather_reduce(out2, sorted_ids, tw, ntp, top_k)
+    return acc.to(out_dtype)
+
+
+# --------------------------------------------------------------------------------------------
+# checkpoint layout -> op layout (load time; integer repacking, any device)
+# --------------------------------------------------------------------------------------------
+def _repack_along_k(codes_nk: torch.Tensor) -> torch.Tensor:
+    """(..., N, K) codes -> (..., N, K/8) int32, nibble j = input channel 8w + j."""
+    c = codes_nk.to(torch.int32) & 0xF
+    out = torch.zeros(c.shape[:-1] + (c.shape[-1] // 8,), dtype=torch.int32, device=c.device)
+    for j in range(8):
+        out |= c[..., j::8] << (4 * j)
+    return out
+
+
+def _pack_along_n(codes_ng: torch.Tensor) -> torch.Tensor:
+    """(..., N, G) codes -> (..., N/8, G) int32, nibble j of word n8 = channel 8*n8 + j."""
+    c = codes_ng.to(torch.int32) & 0xF
+    out = torch.zeros(c.shape[:-2] + (c.shape[-2] // 8, c.shape[-1]), dtype=torch.int32,
+                      device=c.device)
+    for j in range(8):
+        out |= c[..., j::8, :] << (4 * j)
+    return out
+
+
+def _unpack_awq(p: torch.Tensor) -> torch.Tensor:
+    """(..., C/8) int32 in AWQ nibble order -> (..., C) natural-order codes."""
+    shifts = torch.arange(0, 32, 4, dtype=torch.int32, device=p.device)
+    nib = (p.unsqueeze(-1) >> shifts) & 0xF
+    rev = torch.tensor(AWQ_REVERSE_PACK_ORDER, dtype=torch.long, device=p.device)
+    return nib[..., rev].reshape(p.shape[:-1] + (p.shape[-1] * 8,))
+
+
+def awq_moe_to_op_layout(qweight: torch.Tensor, scales: torch.Tensor, qzeros: torch.Tensor):
+    """AWQ MoE (E, K, N/8) + scales (E, G, N) + qzeros (E, G, N/8) ->
+    op layout w (E, N, K/8), scales (E, N, G) fp16, zeros (E, N/8, G)."""
+    w = _repack_along_k(_unpack_awq(qweight).transpose(1, 2))
+    s = scales.transpose(1, 2).contiguous().to(torch.float16)
+    z = _pack_along_n(_unpack_awq(qzeros).transpose(1, 2))
+    return w.contiguous(), s, z.contiguous()
+
+
+def ct_moe_to_op_layout(qweight: torch.Tensor, scales: torch.Tensor):
+    """compressed-tensors GPTQ (E, K/8, N) natural order + scales (E, G, N) ->
+    op layout w (E, N, K/8), scales (E, N, G) fp16 (symmetric uint4b8)."""
+    E, Kp, N = qweight.shape
+    shifts = torch.arange(0, 32, 4, dtype=torch.int32, device=qweight.device)
+    codes = ((qweight.unsqueeze(2) >> shifts.view(1, 1, 8, 1)) & 0xF).reshape(E, Kp * 8, N)
+    w = _repack_along_k(codes.transpose(1, 2))
+    return w.contiguous(), scales.transpose(1, 2).contiguous().to(torch.float16)
+
+
+def wna16_moe_to_op_layout(qweight_u8: torch.Tensor, scales: torch.Tensor,
+                           qzeros_u8: torch.Tensor | None):
+    """MoeWNA16 uint8 storage -> op layout (zero-copy view for the weights).
+    qweight (E, N, K/2) u8 K-packed; qzeros (E, N/2, K/g) u8 N-packed."""
+    w = qweight_u8.contiguous().view(torch.int32)
+    s = scales if scales.dtype == torch.float16 else scales.to(torch.float16)
+    z = None
+    if qzeros_u8 is not None:
+        E, Nh, Kg = qzeros_u8.shape
+        zi = qzeros_u8.contiguous().to(torch.int32).reshape(E, Nh // 4, 4, Kg)
+        z = (zi[:, :, 0] | (zi[:, :, 1] << 8) | (zi[:, :, 2] << 16) | (zi[:, :, 3] << 24))
+        z = z.contiguous()
+    return w, s, z
