@@ -191,12 +191,13 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    replay_stream = torch.cuda.current_stream()  # graph.replay() launches here
     with ClockSampler(local) as clk:
         torch.cuda.synchronize()
-        start.record(stream)
+        start.record(replay_stream)
         for _ in range(args.steps):
             graph.replay()
-        end.record(stream)
+        end.record(replay_stream)
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()

@@ -99,7 +99,7 @@ W4A8_API int w4a8_moe_align_block_size(const int32_t* topk_ids, int64_t num_slot
  * the op mmq_fp8_gemm (bindings.cpp:98-146). kernel: 0 scalar golden, 5/10 tile path, 11 decode
  * GEMV path; every id computes the same function.
  */
-W4A8_API size_t w4a8_mmq_fp8_gemm_workspace_size(int64_t M, int64_t K);
+W4A8_API size_t w4a8_mmq_fp8_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
 W4A8_API int w4a8_mmq_fp8_gemm(const void* x, const int32_t* w_packed, const void* scales,
                       const int32_t* w_zeros, void* out, int64_t M, int64_t N, int64_t K,
                       int64_t group_size, int32_t kernel, int32_t weight_is_e2m1,
@@ -112,7 +112,9 @@ W4A8_API int w4a8_mmq_fp8_gemm(const void* x, const int32_t* w_packed, const voi
  * Replaces launch_mmq_fp8_moe_gemm_gfx1201 (w4a8_fp8_wmma/moe_kernel.hip:1358) behind the op
  * mmq_fp8_moe_gemm (bindings.cpp:178-228). kernel: 0 scalar, 6 tile ("wmma"), 7 GEMV.
  */
-W4A8_API size_t w4a8_moe_gemm_workspace_size(int64_t T, int64_t K);
+/* Workspace of the three grouped GEMM entry points: x_rows = T for mmq_fp8_moe_gemm and
+ * mmq_fp8_moe_gemm1_silu (activations gathered by token), x_rows = P for the scatter op. */
+W4A8_API size_t w4a8_moe_gemm_workspace_size(int64_t x_rows, int64_t P, int64_t N, int64_t K);
 W4A8_API int w4a8_mmq_fp8_moe_gemm(const void* x, const int32_t* w_packed, const void* scales,
                           const int32_t* w_zeros, const int32_t* sorted_token_ids,
                           const int32_t* expert_ids, const int32_t* num_tokens_post_padded,

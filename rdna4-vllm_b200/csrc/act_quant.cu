@@ -23,10 +23,11 @@ __device__ __forceinline__ float warp_max(float v) {
 // Vector path: K % 8 == 0 and 16-byte aligned rows.
 __global__ void __launch_bounds__(kWarpsPerCta * 32)
 act_quant_vec_kernel(const __half* __restrict__ x, uint8_t* __restrict__ xq,
-                     float* __restrict__ scales, int64_t M, int64_t K) {
+                     float* __restrict__ scales, int64_t M, int64_t K,
+                     const int32_t* __restrict__ row_limit) {
     const int lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
-    if (row >= M) return;
+    if (row >= M || (row_limit && row >= row_limit[0])) return;
     const uint4* xr = reinterpret_cast<const uint4*>(x + row * K);
     const int64_t nvec = K / 8;
     float amax = 0.f;
@@ -64,10 +65,11 @@ act_quant_vec_kernel(const __half* __restrict__ x, uint8_t* __restrict__ xq,
 // Scalar path for unaligned rows or K % 8 != 0.
 __global__ void __launch_bounds__(kWarpsPerCta * 32)
 act_quant_scalar_kernel(const __half* __restrict__ x, uint8_t* __restrict__ xq,
-                        float* __restrict__ scales, int64_t M, int64_t K) {
+                        float* __restrict__ scales, int64_t M, int64_t K,
+                        const int32_t* __restrict__ row_limit) {
     const int lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
-    if (row >= M) return;
+    if (row >= M || (row_limit && row >= row_limit[0])) return;
     const __half* xr = x + row * K;
     float amax = 0.f;
     for (int64_t k = lane; k < K; k += 32) amax = fmaxf(amax, fabsf(__half2float(xr[k])));
@@ -81,17 +83,17 @@ act_quant_scalar_kernel(const __half* __restrict__ x, uint8_t* __restrict__ xq,
 }  // namespace
 
 int launch_act_quant(const void* x, uint8_t* xq, float* scales, int64_t M, int64_t K,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, const int32_t* row_limit) {
     if (M <= 0 || K <= 0) return W4A8_OK;
     const dim3 grid((unsigned)((M + kWarpsPerCta - 1) / kWarpsPerCta));
     const bool vec = (K % 8 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
                      ((reinterpret_cast<uintptr_t>(xq) & 7) == 0);
     if (vec)
         act_quant_vec_kernel<<<grid, kWarpsPerCta * 32, 0, stream>>>(
-            static_cast<const __half*>(x), xq, scales, M, K);
+            static_cast<const __half*>(x), xq, scales, M, K, row_limit);
     else
         act_quant_scalar_kernel<<<grid, kWarpsPerCta * 32, 0, stream>>>(
-            static_cast<const __half*>(x), xq, scales, M, K);
+            static_cast<const __half*>(x), xq, scales, M, K, row_limit);
     return launch_status();
 }
 

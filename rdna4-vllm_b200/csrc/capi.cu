@@ -18,24 +18,41 @@ int set_error(const std::string& msg) {
 
 namespace {
 
-struct ActScratch {
+// Scratch layout of every GEMM entry point, in order (each 256-byte aligned):
+//   x_fp8 (rows, K) e4m3 | act_scales (rows,) f32 | xh (rows, K) fp16 | xsum (rows, K/128+1)
+//   float2 | counter | partials
+// xh, xsum and partials are used by the streaming GEMV path only.
+struct Scratch {
     uint8_t* xq;
     float* scales;
+    __half* xh;
+    float2* xsum;
+    int* counter;
+    float* part;
 };
 
-size_t act_scratch_bytes(int64_t rows, int64_t K) {
-    return align_up((size_t)rows * (size_t)K, 256) + align_up((size_t)rows * 4, 256);
+size_t scratch_bytes(int64_t rows, int64_t K, int64_t P, int64_t N) {
+    return align_up((size_t)rows * (size_t)K, 256) + align_up((size_t)rows * 4, 256) +
+           align_up((size_t)rows * (size_t)K * 2, 256) +
+           align_up((size_t)rows * (size_t)(K / 128 + 1) * 8, 256) + 256 +
+           stream_partials_bytes(P, N, K);
 }
 
-bool carve(void* ws, size_t ws_bytes, int64_t rows, int64_t K, ActScratch& s) {
-    if (rows == 0) {
-        s = {nullptr, nullptr};
-        return true;
-    }
-    if (!ws || ws_bytes < act_scratch_bytes(rows, K)) return false;
-    s.xq = static_cast<uint8_t*>(ws);
-    s.scales = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) +
-                                        align_up((size_t)rows * (size_t)K, 256));
+bool carve(void* ws, size_t ws_bytes, int64_t rows, int64_t K, int64_t P, int64_t N,
+           Scratch& s) {
+    if (!ws || ws_bytes < scratch_bytes(rows, K, P, N)) return false;
+    uint8_t* p = static_cast<uint8_t*>(ws);
+    s.xq = p;
+    p += align_up((size_t)rows * (size_t)K, 256);
+    s.scales = reinterpret_cast<float*>(p);
+    p += align_up((size_t)rows * 4, 256);
+    s.xh = reinterpret_cast<__half*>(p);
+    p += align_up((size_t)rows * (size_t)K * 2, 256);
+    s.xsum = reinterpret_cast<float2*>(p);
+    p += align_up((size_t)rows * (size_t)(K / 128 + 1) * 8, 256);
+    s.counter = reinterpret_cast<int*>(p);
+    p += 256;
+    s.part = reinterpret_cast<float*>(p);
     return true;
 }
 
@@ -61,12 +78,12 @@ extern "C" const char* w4a8_last_error(void) { return g_last_error.c_str(); }
 
 extern "C" const char* w4a8_version(void) { return "w4a8_b200 0.1 sm_100a"; }
 
-extern "C" size_t w4a8_mmq_fp8_gemm_workspace_size(int64_t M, int64_t K) {
-    return act_scratch_bytes(M, K);
+extern "C" size_t w4a8_mmq_fp8_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
+    return scratch_bytes(M, K, M, N);
 }
 
-extern "C" size_t w4a8_moe_gemm_workspace_size(int64_t T, int64_t K) {
-    return act_scratch_bytes(T, K);
+extern "C" size_t w4a8_moe_gemm_workspace_size(int64_t x_rows, int64_t P, int64_t N, int64_t K) {
+    return scratch_bytes(x_rows, K, P, N);
 }
 
 extern "C" int w4a8_mmq_fp8_gemm(const void* x, const int32_t* w_packed, const void* scales,
@@ -92,10 +109,39 @@ extern "C" int w4a8_mmq_fp8_gemm(const void* x, const int32_t* w_packed, const v
     if (M > INT32_MAX / 2 || N > INT32_MAX / 2) return set_error("mmq_fp8_gemm: size overflow");
     if (M == 0) return W4A8_OK;
     if (!x || !w_packed || !scales || !out) return set_error("mmq_fp8_gemm: null pointer");
-    ActScratch s;
-    if (!carve(workspace, workspace_bytes, M, K, s))
+    Scratch s;
+    if (!carve(workspace, workspace_bytes, M, K, M, N, s))
         return set_error("mmq_fp8_gemm: workspace too small");
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int G = (int)(K / group_size);
+    const bool stream_path = kernel != W4A8_DENSE_REFERENCE_SCALAR && M <= 32 &&
+                             stream_path_ok(K, G, weight_is_e2m1, w_packed);
+    if (stream_path) {
+        if (int rc = launch_operand_quant(x, OperandOut{s.xq, s.scales, s.xh, s.xsum}, M, K,
+                                          nullptr, st))
+            return rc;
+        StreamArgs sa{};
+        sa.xh = s.xh;
+        sa.xsum = s.xsum;
+        sa.act_scales = s.scales;
+        sa.w = w_packed;
+        sa.scales = static_cast<const __half*>(scales);
+        sa.zeros = w_zeros;
+        sa.out16 = static_cast<__half*>(out);
+        sa.part = s.part;
+        sa.counter = s.counter;
+        sa.K = K;
+        sa.N = (int)N;
+        sa.G = G;
+        sa.E = 1;
+        sa.P = (int)M;
+        sa.num_valid = (int)M;
+        sa.top_k = 1;
+        sa.out_top_k = 1;
+        sa.block_m = 1 << 20;
+        sa.mode = kStreamStore;
+        return launch_w4_stream(sa, st);
+    }
     if (int rc = launch_act_quant(x, s.xq, s.scales, M, K, st)) return rc;
     GemmArgs a{};
     a.x_fp8 = s.xq;
@@ -106,7 +152,7 @@ extern "C" int w4a8_mmq_fp8_gemm(const void* x, const int32_t* w_packed, const v
     a.out16 = static_cast<__half*>(out);
     a.K = K;
     a.N = (int)N;
-    a.G = (int)(K / group_size);
+    a.G = G;
     a.E = 1;
     a.P = (int)M;
     a.num_valid = (int)M;
@@ -158,11 +204,53 @@ int moe_launch(const char* op, int epi, const void* x, const int32_t* w_packed,
         }())
         return st0;
     if (P == 0) return W4A8_OK;
-    ActScratch s;
-    if (!carve(ws, ws_bytes, x_rows, K, s)) return set_error(o + ": workspace too small");
+    Scratch s;
+    if (!carve(ws, ws_bytes, x_rows, K, P, N, s)) return set_error(o + ": workspace too small");
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int G = (int)(K / group_size);
+    const bool stream_path = kernel == W4A8_MOE_GEMV && stream_path_ok(K, G, e2m1, w_packed);
+    const int32_t* row_limit = (epi == kEpiScatter) ? ntp : nullptr;
+    if (stream_path) {
+        if (int rc = launch_operand_quant(x, OperandOut{s.xq, s.scales, s.xh, s.xsum}, x_rows, K,
+                                          row_limit, st))
+            return rc;
+        StreamArgs sa{};
+        sa.xh = s.xh;
+        sa.xsum = s.xsum;
+        sa.act_scales = s.scales;
+        sa.w = w_packed;
+        sa.scales = static_cast<const __half*>(scales);
+        sa.zeros = w_zeros;
+        sa.sorted_ids = sorted_ids;
+        sa.expert_ids = expert_ids;
+        sa.ntp = ntp;
+        sa.topk_weights = topk_weights;
+        sa.part = s.part;
+        sa.counter = s.counter;
+        sa.K = K;
+        sa.N = (int)N;
+        sa.G = G;
+        sa.E = (int)E;
+        sa.P = (int)P;
+        sa.block_m = (int)block_m;
+        if (epi == kEpiScatter) {
+            sa.out32 = static_cast<float*>(out);
+            sa.src_identity = 1;
+            sa.num_valid = (int)(M_out * top_k);
+            sa.top_k = 1;
+            sa.out_top_k = (int)top_k;
+            sa.mode = kStreamScatter;
+        } else {
+            sa.out16 = static_cast<__half*>(out);
+            sa.num_valid = (int)(x_rows * top_k);
+            sa.top_k = (int)top_k;
+            sa.out_top_k = (int)top_k;
+            sa.mode = epi == kEpiSilu ? kStreamSilu : kStreamStore;
+        }
+        return launch_w4_stream(sa, st);
+    }
     if (x_rows > 0)
-        if (int rc = launch_act_quant(x, s.xq, s.scales, x_rows, K, st)) return rc;
+        if (int rc = launch_act_quant(x, s.xq, s.scales, x_rows, K, st, row_limit)) return rc;
     GemmArgs a{};
     a.x_fp8 = s.xq;
     a.act_scales = s.scales;
@@ -175,7 +263,7 @@ int moe_launch(const char* op, int epi, const void* x, const int32_t* w_packed,
     a.topk_weights = topk_weights;
     a.K = K;
     a.N = (int)N;
-    a.G = (int)(K / group_size);
+    a.G = G;
     a.E = (int)E;
     a.P = (int)P;
     a.block_m = (int)block_m;

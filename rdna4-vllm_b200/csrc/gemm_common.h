@@ -40,9 +40,55 @@ struct GemmArgs {
     int src_identity;
     int e2m1;
     int kc;         // activation chunk (set by the launcher)
+    int info_off;   // byte offset of the per-row table in dynamic shared memory (launcher)
 };
 
 bool mma_path_ok(const GemmArgs& a);
+
+// ---- persistent streaming GEMV (gemv_stream.cu) ----
+enum StreamMode : int {
+    kStreamStore = 0,      // out16[r, n] = fp16(acc * a_scale)
+    kStreamSilu = 1,       // out16[r, n] = silu_and_mul(gate n, up n + N/2)   (N/2 columns)
+    kStreamScatter = 2,    // out32[sid / out_top_k, n] += topk_w[sid] * acc * a_scale
+    kStreamSiluQuant = 3,  // finish only: SiLU row, then quantise it as the next GEMM's operand
+};
+
+// Output block of the operand quantiser (e4m3 bytes, scales, fp16 operand copy, group sums).
+struct OperandOut {
+    uint8_t* xq;
+    float* scales;
+    __half* xh;
+    float2* xsum;
+};
+
+struct StreamArgs {
+    const __half* xh;           // (rows, K) fp16 operand copy of the e4m3 activations
+    const float2* xsum;         // (rows, G) per-group {K0, S} activation sums (see gemv_stream.cu)
+    const float* act_scales;    // (rows,)
+    const int32_t* w;
+    const __half* scales;
+    const int32_t* zeros;
+    const int32_t* sorted_ids;
+    const int32_t* expert_ids;
+    const int32_t* ntp;
+    const float* topk_weights;
+    __half* out16;
+    float* out32;
+    float* part;                // fp32 partials [ks][P][N]
+    int* counter;               // unused by the static schedule; kept zero
+    int64_t K;
+    int N, G, E, P, num_valid, top_k, out_top_k, block_m, src_identity, mode;
+    int ks_n, rg_n, force_part; // set by the launcher
+    OperandOut next;            // kStreamSiluQuant: where the quantised SiLU rows go
+    __half* out_silu;           // kStreamSiluQuant: optional fp16 SiLU rows (P, N/2)
+};
+
+bool stream_path_ok(int64_t K, int G, int e2m1, const void* w);
+size_t stream_partials_bytes(int64_t P, int64_t N, int64_t K);
+int launch_w4_stream(StreamArgs a, cudaStream_t stream);
+// Quantise rows [0, min(M, row_limit)) of x (fp16) into the streaming GEMV operand format.
+int launch_operand_quant(const void* x, OperandOut o, int64_t M, int64_t K,
+                         const int32_t* row_limit, cudaStream_t stream);
 int launch_w4_gemm(GemmArgs a, int epi, int row_tile, bool scalar, int64_t est_rows,
                    cudaStream_t stream);
 

@@ -174,17 +174,6 @@ __device__ __forceinline__ void fill_act_tile(const GemmArgs& a, const RowInfo* 
     }
 }
 
-__device__ __forceinline__ __half silu_and_mul_h(float gate_f, float up_f) {
-    // vLLM silu_and_mul on fp16 tensors: the gate/up values are the fp16 gemm1 stores, silu is
-    // evaluated in fp32 and rounded to fp16, the product is a half*half multiply
-    // (mirrors moe_silu_and_mul_h, w4a8_fp8_wmma/moe_kernel.hip:555-565).
-    const __half gh = __float2half_rn(gate_f);
-    const __half uh = __float2half_rn(up_f);
-    const float g = __half2float(gh);
-    const __half sh = __float2half_rn(__fdiv_rn(g, 1.0f + expf(-g)));
-    return __hmul(sh, uh);
-}
-
 template <int NT, int WK, int EPI>
 __global__ void __launch_bounds__(kNW * WK * 32)
 w4_mma_kernel(const GemmArgs a) {
@@ -201,7 +190,7 @@ w4_mma_kernel(const GemmArgs a) {
     const int kc = a.kc;
     const int row_stride = kc * 2 + 32;
     uint8_t* act_tile = smem;
-    RowInfo* info = reinterpret_cast<RowInfo*>(smem + R * row_stride);
+    RowInfo* info = reinterpret_cast<RowInfo*>(smem + a.info_off);
     __shared__ int any_valid;
     __shared__ int expert_sh;
     if (threadIdx.x == 0) {
@@ -285,7 +274,7 @@ w4_mma_kernel(const GemmArgs a) {
     }
 
     // Split-K reduction across the WK warps sharing (wn): fixed order wk = 0..WK-1.
-    if (WK > 1) {
+    if constexpr (WK > 1) {
         __syncthreads();
         float* red = reinterpret_cast<float*>(smem);  // reuse the activation tile
         constexpr int per_thread = NT * 4 * (kSilu ? 2 : 1);
@@ -332,7 +321,7 @@ w4_mma_kernel(const GemmArgs a) {
                 if (a.ntp && r >= a.ntp[0]) continue;
                 __half v = __float2half_rn(0.f);
                 if (ri.src >= 0)
-                    v = silu_and_mul_h(tot[t][j] * ri.ascale, totu[t][j] * ri.ascale);
+                    v = silu_and_mul_half(tot[t][j] * ri.ascale, totu[t][j] * ri.ascale);
                 a.out16[(int64_t)r * n_out + n] = v;
             } else {
                 if (a.ntp && r >= a.ntp[0]) continue;
@@ -395,7 +384,7 @@ w4_scalar_kernel(const GemmArgs a) {
         const int token = sid / a.out_top_k;
         atomicAdd(a.out32 + (int64_t)token * a.N + n, a.topk_weights[sid] * res[0] * asc);
     } else if (kSilu) {
-        a.out16[(int64_t)r * n_out + n] = silu_and_mul_h(res[0] * asc, res[1] * asc);
+        a.out16[(int64_t)r * n_out + n] = silu_and_mul_half(res[0] * asc, res[1] * asc);
     } else {
         a.out16[(int64_t)r * n_out + n] = __float2half_rn(res[0] * asc);
     }
@@ -409,12 +398,15 @@ int launch_mma_t(GemmArgs a, cudaStream_t stream) {
     while (a.K % kc) kc -= 128;  // chunks tile K exactly
     a.kc = kc;
     const int row_stride = kc * 2 + 32;
-    size_t smem = (size_t)R * row_stride + R * sizeof(RowInfo);
-    if constexpr (WK > 1) {
+    // Region 0 holds the activation tile and, after the main loop, the split-K partials.
+    size_t region = (size_t)R * row_stride;
+    if (WK > 1) {
         const size_t red = (size_t)(WK - 1) * kNW * 32 * NT * 4 * (EPI == kEpiSilu ? 2 : 1) * 4;
-        // The reduction buffer overlays the activation tile; RowInfo stays after it.
-        if (red > (size_t)R * row_stride) return set_error("internal: split-K buffer overflow");
+        region = std::max(region, red);
     }
+    region = align_up(region, 16);
+    a.info_off = (int)region;
+    const size_t smem = region + R * sizeof(RowInfo);
     auto kern = w4_mma_kernel<NT, WK, EPI>;
     if (smem > 48 * 1024)
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

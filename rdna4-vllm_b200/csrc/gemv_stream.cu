@@ -1,0 +1,513 @@
+// gemv_stream.cu — persistent W4A8 GEMV for decode-sized row counts.
+//
+// Work item = (8-row block b of the padded-sorted rows, K split ks of 4 groups, 128-row group
+// rg of the weight rows). CTAs (8 warps, 2 per SM) walk items round-robin; warp w computes the
+// 16 weight rows rg*128 + 16w .. +15 of an item. While item i is computed the CTA has already
+// issued item i+1's weight loads (register double buffer of 128-bit non-allocating loads) and
+// its activation tile, group scales, zero points and activation group sums (cp.async into the
+// other half of a shared double buffer); warp 0 meanwhile fetches item i+2's routing rows.
+//
+// Arithmetic. Per 128-code group a lane expands 2 weight rows x 32 codes with the fp16
+// magic-number trick without subtracting the zero point: pairs (0,4),(2,6) of every 8-code word
+// become 1024 + q and pairs (1,5),(3,7) become 1024 + 16q, all exact in fp16. The activation
+// operand (fp16 copies of the e4m3 bytes, exact) carries a / 16 at the (1,5),(3,7) positions
+// (exact: a power-of-two scale), so one mma.sync.m16n8k16 (fp16 x fp16 -> fp32) chain yields
+//     acc = sum_k q_k a_k + K0,   K0 = 1024 * sum_{even pairs} a + 64 * sum_{odd pairs} a.
+// With S = sum_k a_k the group result is sum_k (q_k - z) a_k = acc - K0 - z*S; it is folded as
+//     tot += scale[n,g] * (acc - K0 - z*S)
+// and multiplied by the row's activation scale in the epilogue: the reference's per-group fp32
+// association (w4a8_fp8_wmma/test_correctness.py:113-119). K0 and S are per (activation row,
+// group) sums computed once by the operand quantiser. The 1024-offset terms are removed in
+// fp32, which leaves a relative error near 1e-4 of the group sum (well inside the 1e-2 bar).
+//
+// K splits write fp32 partials [ks][row][n]; w4_stream_finish_kernel sums them in fixed order
+// (results do not depend on scheduling) and applies the epilogue. One split: direct epilogue.
+#include <algorithm>
+
+#include "common.cuh"
+#include "gemm_common.h"
+#include "internal.h"
+
+namespace w4a8 {
+
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kSpi = 4;                          // K blocks (groups of 128) per item
+constexpr int kRowsPerItem = kWarps * 16;        // 128 weight rows
+constexpr int kActStride = kSpi * 256 + 32;      // bytes per activation row in shared memory
+
+__device__ __forceinline__ int act_off(int kb, int c, int u) {
+    return kb * 256 + c * 64 + ((u ^ ((c >> 1) & 1)) << 4);
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
+    const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+    const int n = pred ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(n));
+}
+__device__ __forceinline__ void cp_async8(void* smem, const void* gmem, bool pred) {
+    const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+    const int n = pred ? 8 : 0;
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(s), "l"(gmem), "r"(n));
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::); }
+
+struct ItemMeta {
+    int item;     // item index (>= total: none)
+    int any;      // 1 when at least one of the 8 rows is live
+    int e;        // expert
+    int b, ks, rg;
+    int src[8];   // activation row per token column (-1: padding)
+    int sid[8];
+};
+
+struct Smem {
+    uint8_t act[2][8][kActStride];
+    float2 xs[2][kSpi][8];                   // {K0, S} per (group, token column)
+    __half sc[2][kRowsPerItem][kSpi];
+    uint32_t zr[2][kRowsPerItem / 8][kSpi];
+    ItemMeta meta[3];
+};
+
+// 8 codes of one word -> 4 half2 (pairs (0,4),(1,5),(2,6),(3,7)): 1024+q and 1024+16q.
+__device__ __forceinline__ void expand_word(uint32_t w, uint32_t (&h)[4]) {
+    constexpr uint32_t kMagic = 0x64006400u;
+    const uint32_t w8 = w >> 8;
+    h[0] = and_or(w, 0x000F000Fu, kMagic);
+    h[1] = and_or(w, 0x00F000F0u, kMagic);
+    h[2] = and_or(w8, 0x000F000Fu, kMagic);
+    h[3] = and_or(w8, 0x00F000F0u, kMagic);
+}
+
+// Item metadata is produced by warp 0 in two halves so that its L2 latency hides under the
+// warp's own compute: meta_issue() loads the raw routing values into registers, and
+// meta_publish() (after the compute) derives the rows and writes the shared slot.
+struct MetaRegs {
+    int item, e, sid;
+};
+
+__device__ __forceinline__ MetaRegs meta_issue(const StreamArgs& a, int item, int total,
+                                               int per_b, int P_valid) {
+    const int lane = threadIdx.x & 31;
+    MetaRegs r{item, -1, -1};
+    if (item < total) {
+        const int row = (item / per_b) * 8 + lane;
+        if (lane < 8 && row < P_valid) r.sid = a.sorted_ids ? a.sorted_ids[row] : row;
+        r.e = a.expert_ids ? a.expert_ids[((item / per_b) * 8) / a.block_m] : 0;
+    }
+    return r;
+}
+
+__device__ __forceinline__ void meta_publish(const StreamArgs& a, const MetaRegs& r, int total,
+                                             int per_b, ItemMeta& m) {
+    const int lane = threadIdx.x & 31;
+    const bool live = r.item < total && r.e >= 0 && r.e < a.E;
+    const bool ok = live && lane < 8 && r.sid >= 0 && r.sid < a.num_valid;
+    const int any = __any_sync(0xffffffffu, ok);
+    if (lane < 8) {
+        m.src[lane] = ok ? (a.src_identity ? (r.item / per_b) * 8 + lane : r.sid / a.top_k) : -1;
+        m.sid[lane] = ok ? r.sid : 0;
+    }
+    if (lane == 0) {
+        const int b = r.item / per_b, rem = r.item - b * per_b;
+        m.item = r.item;
+        m.any = any;
+        m.e = r.e;
+        m.b = b;
+        m.ks = rem / a.rg_n;
+        m.rg = rem - m.ks * a.rg_n;
+    }
+}
+
+// All threads: cp.async the activation tile, group sums, scales and zero points of a live
+// item into buffer `buf`.
+__device__ __forceinline__ void stage_item(const StreamArgs& a, Smem& sm, const ItemMeta& m,
+                                           int buf) {
+    const int tid = threadIdx.x;
+    const int64_t k0 = (int64_t)m.ks * kSpi * 128;
+    const int kb0 = m.ks * kSpi;
+    for (int idx = tid; idx < 8 * 64; idx += blockDim.x) {  // 8 rows x 512 fp16
+        const int row = idx >> 6, q = idx & 63;
+        const int src = m.src[row];
+        const __half* g = a.xh + (int64_t)max(src, 0) * a.K + k0 + q * 8;
+        cp_async16(&sm.act[buf][row][act_off(q >> 4, (q >> 2) & 3, q & 3)], g, src >= 0);
+    }
+    const int n0 = m.rg * kRowsPerItem;
+    if (tid < kRowsPerItem) {  // scales: 128 rows x 4 groups
+        const int n = n0 + tid;
+        const bool ok = n < a.N;
+        const __half* g = a.scales + ((int64_t)m.e * a.N + (ok ? n : 0)) * a.G + kb0;
+        cp_async8(&sm.sc[buf][tid][0], g, ok);
+    } else if (tid < kRowsPerItem + kRowsPerItem / 8) {  // zero points: 16 words x 4 groups
+        const int j = tid - kRowsPerItem;
+        const int n8 = n0 / 8 + j;
+        if (a.zeros && n8 < a.N / 8)
+            cp_async16(&sm.zr[buf][j][0], a.zeros + ((int64_t)m.e * (a.N / 8) + n8) * a.G + kb0,
+                       true);
+    } else if (tid < kRowsPerItem + kRowsPerItem / 8 + 32) {  // group sums: 4 groups x 8 rows
+        const int j = tid - kRowsPerItem - kRowsPerItem / 8;
+        const int grp = j >> 3, col = j & 7;
+        const int src = m.src[col];
+        const float2* g = a.xsum + (int64_t)max(src, 0) * a.G + kb0 + grp;
+        cp_async8(&sm.xs[buf][grp][col], g, src >= 0);
+    }
+    asm volatile("cp.async.commit_group;" ::);
+}
+
+struct WeightRegs {
+    uint4 w[kSpi][2];
+};
+
+__device__ __forceinline__ void load_weights(const StreamArgs& a, const ItemMeta& m, int warp,
+                                             int lane, WeightRegs& r) {
+    const int64_t kw = a.K / 8;
+    const int n0 = m.rg * kRowsPerItem + warp * 16 + (lane >> 2);
+    const int row0 = min(n0, a.N - 1), row1 = min(n0 + 8, a.N - 1);
+    const int32_t* base = a.w + (int64_t)m.e * a.N * kw + (m.ks * kSpi) * 16 + (lane & 3) * 4;
+#pragma unroll
+    for (int j = 0; j < kSpi; ++j) {
+        if (m.ks * kSpi + j < a.G) {
+            r.w[j][0] = ldg_stream(base + (int64_t)row0 * kw + j * 16);
+            r.w[j][1] = ldg_stream(base + (int64_t)row1 * kw + j * 16);
+        } else {
+            r.w[j][0] = r.w[j][1] = make_uint4(0, 0, 0, 0);
+        }
+    }
+}
+
+// Compute one item from registers + shared buffer `buf`; emit partials or the epilogue.
+__device__ __forceinline__ void compute_item(const StreamArgs& a, const Smem& sm,
+                                             const ItemMeta& m, int buf, int warp, int lane,
+                                             const WeightRegs& r) {
+    const int c = lane & 3, tok = lane >> 2;
+    const int nl = warp * 16 + tok;              // local row (0..127) of the item
+    const int n0 = m.rg * kRowsPerItem + nl;
+    if (m.rg * kRowsPerItem + warp * 16 >= a.N) return;   // warp beyond N
+    float tot[4] = {0.f, 0.f, 0.f, 0.f};
+    if (!m.any) {
+        // all-padding block or non-local expert: rows are zeros for the direct store epilogue
+        if (a.mode == kStreamStore && !a.force_part) {
+            const int P_valid = a.ntp ? min(a.ntp[0], a.P) : a.P;
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                const int rr = m.b * 8 + 2 * c + (jj & 1), n = n0 + (jj >> 1) * 8;
+                if (rr < P_valid && n < a.N) a.out16[(int64_t)rr * a.N + n] = __float2half_rn(0.f);
+            }
+        }
+        return;
+    }
+    const uint8_t* rowp = &sm.act[buf][tok][0];
+    const int sh0 = (n0 & 7) * 4, sh1 = ((n0 + 8) & 7) * 4;
+#pragma unroll
+    for (int j = 0; j < kSpi; ++j) {
+        if (m.ks * kSpi + j >= a.G) break;
+        const uint32_t w0[4] = {r.w[j][0].x, r.w[j][0].y, r.w[j][0].z, r.w[j][0].w};
+        const uint32_t w1[4] = {r.w[j][1].x, r.w[j][1].y, r.w[j][1].z, r.w[j][1].w};
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            uint32_t h0[4], h1[4];
+            expand_word(w0[i], h0);
+            expand_word(w1[i], h1);
+            const uint4 bq = *reinterpret_cast<const uint4*>(rowp + act_off(j, c, i));
+            const uint32_t a0[4] = {h0[0], h1[0], h0[1], h1[1]};
+            mma_16816(acc, a0, bq.x, bq.y);
+            const uint32_t a1[4] = {h0[2], h1[2], h0[3], h1[3]};
+            mma_16816(acc, a1, bq.z, bq.w);
+        }
+        float z0 = 8.f, z1 = 8.f;
+        if (a.zeros) {
+            z0 = (float)((sm.zr[buf][nl >> 3][j] >> sh0) & 0xF);
+            z1 = (float)((sm.zr[buf][(nl + 8) >> 3][j] >> sh1) & 0xF);
+        }
+        const float4 xs = *reinterpret_cast<const float4*>(&sm.xs[buf][j][2 * c]);  // K0,S x 2 cols
+        const float s0 = __half2float(sm.sc[buf][nl][j]);
+        const float s1 = __half2float(sm.sc[buf][nl + 8][j]);
+        tot[0] = fmaf(s0, fmaf(-z0, xs.y, acc[0] - xs.x), tot[0]);
+        tot[1] = fmaf(s0, fmaf(-z0, xs.w, acc[1] - xs.z), tot[1]);
+        tot[2] = fmaf(s1, fmaf(-z1, xs.y, acc[2] - xs.x), tot[2]);
+        tot[3] = fmaf(s1, fmaf(-z1, xs.w, acc[3] - xs.z), tot[3]);
+    }
+    // tot[0..1]: row n0, token columns 2c, 2c+1; tot[2..3]: row n0 + 8.
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+        const int col = 2 * c + (jj & 1);
+        const int n = n0 + (jj >> 1) * 8;
+        if (n >= a.N) continue;
+        const int src = m.src[col];
+        const int rr = m.b * 8 + col;
+        if (a.force_part) {
+            if (src >= 0) a.part[((int64_t)m.ks * a.P + rr) * a.N + n] = tot[jj];
+        } else if (a.mode == kStreamScatter) {
+            if (src >= 0) {
+                const int sid = m.sid[col];
+                atomicAdd(a.out32 + (int64_t)(sid / a.out_top_k) * a.N + n,
+                          a.topk_weights[sid] * tot[jj] * a.act_scales[src]);
+            }
+        } else {  // store
+            const int P_valid = a.ntp ? min(a.ntp[0], a.P) : a.P;
+            if (rr < P_valid)
+                a.out16[(int64_t)rr * a.N + n] =
+                    __float2half_rn(src >= 0 ? tot[jj] * a.act_scales[src] : 0.f);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kWarps * 32, 2) w4_stream_kernel(const StreamArgs a) {
+    __shared__ __align__(16) Smem sm;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int P_valid = a.ntp ? min(a.ntp[0], a.P) : a.P;
+    const int per_b = a.ks_n * a.rg_n;
+    const int total = ((P_valid + 7) / 8) * per_b;
+    // Static round-robin schedule: this CTA's i-th item is blockIdx.x + i * gridDim.x.
+    const int stride = gridDim.x;
+    int item = blockIdx.x;
+    if (item >= total) return;
+    if (warp == 0) {
+        meta_publish(a, meta_issue(a, item, total, per_b, P_valid), total, per_b, sm.meta[0]);
+        meta_publish(a, meta_issue(a, item + stride, total, per_b, P_valid), total, per_b,
+                     sm.meta[1]);
+    }
+    __syncthreads();
+    WeightRegs r0, r1;
+    if (sm.meta[0].any) {
+        load_weights(a, sm.meta[0], warp, lane, r0);
+        stage_item(a, sm, sm.meta[0], 0);
+    }
+    // Iteration i computes item i (shared buffer i%2, meta slot i%3, registers r[i%2]); it first
+    // issues item i+1's loads and warp 0 prepares item i+2's metadata. One barrier per item:
+    // it publishes item i's staged tile and item i+1's metadata, and retires item i-1's buffer.
+    int i = 0;
+    while (true) {
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            const int buf = half;
+            cp_async_wait_all();
+            __syncthreads();
+            const ItemMeta& cur = sm.meta[i % 3];
+            const ItemMeta& nxt = sm.meta[(i + 1) % 3];
+            const bool has_next = nxt.item < total;
+            if (has_next && nxt.any) {  // empty items stage nothing (their expert may be -1)
+                load_weights(a, nxt, warp, lane, half == 0 ? r1 : r0);
+                stage_item(a, sm, nxt, buf ^ 1);
+            }
+            MetaRegs mr{};
+            if (warp == 0) mr = meta_issue(a, item + 2 * stride, total, per_b, P_valid);
+            compute_item(a, sm, cur, buf, warp, lane, half == 0 ? r0 : r1);
+            if (warp == 0) meta_publish(a, mr, total, per_b, sm.meta[(i + 2) % 3]);
+            item += stride;
+            ++i;
+            if (!has_next) {
+                cp_async_wait_all();
+                return;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// Operand quantiser: one CTA per row. Writes the e4m3 bytes and the scale (the oracle's
+// divide-based rounding, test_correctness.py:74-76), the fp16 operand copy (pairs
+// (0,4),(1,5),(2,6),(3,7) per 8-code unit, the (1,5),(3,7) pairs divided by 16) and the per
+// 128-group sums {K0, S}. The row's values come from `src` (global or shared memory).
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    if (w == 0) {
+        v = l < (int)(blockDim.x >> 5) ? red[l] : 0.f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (l == 0) red[0] = v;
+    }
+    __syncthreads();
+    const float r = red[0];
+    __syncthreads();
+    return r;
+}
+
+__device__ void quant_operand_row(const __half* src, int64_t K, int64_t row, const OperandOut& o,
+                                  float* red) {
+    float amax = 0.f;
+    const int64_t nchunk = K / 8;
+    for (int64_t i = threadIdx.x; i < nchunk; i += blockDim.x) {
+        const uint4 v = *reinterpret_cast<const uint4*>(src + i * 8);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const __half2 h = __habs2(*reinterpret_cast<const __half2*>(&w[j]));
+            amax = fmaxf(amax, fmaxf(__low2float(h), __high2float(h)));
+        }
+    }
+    amax = block_max(amax, red);
+    const float s = __fdiv_rn(fmaxf(amax, kAmaxFloor), kE4m3Max);
+    if (threadIdx.x == 0) o.scales[row] = s;
+    const int G = (int)(K / 128);
+    // chunk i belongs to group i / 16; the 16 chunks of a group sit in 16 consecutive lanes
+    for (int64_t i0 = 0; i0 < nchunk; i0 += blockDim.x) {
+        const int64_t i = i0 + threadIdx.x;
+        float se = 0.f, so = 0.f;
+        if (i < nchunk) {
+            const uint4 v = *reinterpret_cast<const uint4*>(src + i * 8);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+            uint32_t q[2];
+#pragma unroll
+            for (int j = 0; j < 4; j += 2) {
+                const __half2 h0 = *reinterpret_cast<const __half2*>(&w[j]);
+                const __half2 h1 = *reinterpret_cast<const __half2*>(&w[j + 1]);
+                const uint16_t p0 = f32x2_to_e4m3x2(__fdiv_rn(__low2float(h0), s),
+                                                    __fdiv_rn(__high2float(h0), s));
+                const uint16_t p1 = f32x2_to_e4m3x2(__fdiv_rn(__low2float(h1), s),
+                                                    __fdiv_rn(__high2float(h1), s));
+                q[j / 2] = (uint32_t)p0 | ((uint32_t)p1 << 16);
+            }
+            if (o.xq) reinterpret_cast<uint2*>(o.xq + row * K)[i] = make_uint2(q[0], q[1]);
+            const uint32_t pe = prmt(q[0], q[1], 0x5140u);  // bytes b0 b4 b1 b5
+            const uint32_t po = prmt(q[0], q[1], 0x7362u);  // bytes b2 b6 b3 b7
+            const uint32_t h04 = e4m3x2_to_f16x2((uint16_t)(pe & 0xffff));
+            const uint32_t h15 = e4m3x2_to_f16x2((uint16_t)(pe >> 16));
+            const uint32_t h26 = e4m3x2_to_f16x2((uint16_t)(po & 0xffff));
+            const uint32_t h37 = e4m3x2_to_f16x2((uint16_t)(po >> 16));
+            const __half2 sixteenth = __float2half2_rn(0.0625f);
+            const __half2 d15 = __hmul2(*reinterpret_cast<const __half2*>(&h15), sixteenth);
+            const __half2 d37 = __hmul2(*reinterpret_cast<const __half2*>(&h37), sixteenth);
+            uint4 out;
+            out.x = h04;
+            out.y = *reinterpret_cast<const uint32_t*>(&d15);
+            out.z = h26;
+            out.w = *reinterpret_cast<const uint32_t*>(&d37);
+            reinterpret_cast<uint4*>(o.xh + row * K)[i] = out;
+            const float2 f04 = __half22float2(*reinterpret_cast<const __half2*>(&h04));
+            const float2 f26 = __half22float2(*reinterpret_cast<const __half2*>(&h26));
+            const float2 f15 = __half22float2(*reinterpret_cast<const __half2*>(&h15));
+            const float2 f37 = __half22float2(*reinterpret_cast<const __half2*>(&h37));
+            se = (f04.x + f04.y) + (f26.x + f26.y);
+            so = (f15.x + f15.y) + (f37.x + f37.y);
+        }
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) {
+            se += __shfl_xor_sync(0xffffffffu, se, off);
+            so += __shfl_xor_sync(0xffffffffu, so, off);
+        }
+        if ((threadIdx.x & 15) == 0 && i < nchunk) {
+            const int64_t g = i / 16;
+            if (g < G) o.xsum[row * G + g] = make_float2(1024.f * se + 64.f * so, se + so);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) operand_quant_kernel(const __half* __restrict__ x,
+                                                            OperandOut o, int64_t M, int64_t K,
+                                                            const int32_t* row_limit) {
+    __shared__ float red[32];
+    const int64_t row = blockIdx.x;
+    if (row >= M || (row_limit && row >= row_limit[0])) return;
+    quant_operand_row(x + row * K, K, row, o, red);
+}
+
+// ---------------------------------------------------------------------------------------
+// Finish: sum the K-split partials in fixed order and apply the epilogue. One CTA per row.
+// kStreamSiluQuant additionally quantises the SiLU row as the next GEMM's operand.
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) w4_stream_finish_kernel(const StreamArgs a) {
+    extern __shared__ __align__(16) __half silu_row[];
+    __shared__ float red[32];
+    const int r = blockIdx.x;
+    const int P_valid = a.ntp ? min(a.ntp[0], a.P) : a.P;
+    if (r >= P_valid) return;
+    const int sid = a.sorted_ids ? a.sorted_ids[r] : r;
+    const int e = a.expert_ids ? a.expert_ids[r / a.block_m] : 0;
+    const bool valid = sid >= 0 && sid < a.num_valid && e >= 0 && e < a.E;
+    const int src = valid ? (a.src_identity ? r : sid / a.top_k) : -1;
+    const float asc = valid ? a.act_scales[src] : 0.f;
+    const bool silu = a.mode == kStreamSilu || a.mode == kStreamSiluQuant;
+    const int n_out = silu ? a.N / 2 : a.N;
+    for (int n = threadIdx.x; n < n_out; n += blockDim.x) {
+        __half hv = __float2half_rn(0.f);
+        if (valid) {
+            float v = 0.f, u = 0.f;
+            for (int ks = 0; ks < a.ks_n; ++ks) {
+                const float* p = a.part + ((int64_t)ks * a.P + r) * a.N;
+                v += p[n];
+                if (silu) u += p[n + n_out];
+            }
+            if (silu) {
+                hv = silu_and_mul_half(v * asc, u * asc);
+            } else if (a.mode == kStreamScatter) {
+                atomicAdd(a.out32 + (int64_t)(sid / a.out_top_k) * a.N + n,
+                          a.topk_weights[sid] * v * asc);
+                continue;
+            } else {
+                hv = __float2half_rn(v * asc);
+            }
+        } else if (a.mode == kStreamScatter) {
+            continue;
+        }
+        if (a.mode == kStreamSiluQuant) {
+            silu_row[n] = hv;
+            if (a.out_silu) a.out_silu[(int64_t)r * n_out + n] = hv;
+        } else {
+            a.out16[(int64_t)r * n_out + n] = hv;
+        }
+    }
+    if (a.mode == kStreamSiluQuant) {
+        __syncthreads();
+        quant_operand_row(silu_row, n_out, r, a.next, red);
+    }
+}
+
+}  // namespace
+
+bool stream_path_ok(int64_t K, int G, int e2m1, const void* w) {
+    return !e2m1 && G > 0 && K == (int64_t)G * 128 && (G % kSpi) == 0 &&
+           (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+}
+
+size_t stream_partials_bytes(int64_t P, int64_t N, int64_t K) {
+    const int64_t G = std::max<int64_t>(K / 128, 1);
+    const int64_t ks = (G + kSpi - 1) / kSpi;
+    return align_up((size_t)(ks * P * N) * 4, 256);
+}
+
+int launch_operand_quant(const void* x, OperandOut o, int64_t M, int64_t K,
+                         const int32_t* row_limit, cudaStream_t stream) {
+    if (M <= 0) return W4A8_OK;
+    if (K % 128 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0)
+        return set_error("operand quant needs K % 128 == 0 and 16-byte aligned rows");
+    operand_quant_kernel<<<(unsigned)M, 256, 0, stream>>>(static_cast<const __half*>(x), o, M, K,
+                                                         row_limit);
+    return launch_status();
+}
+
+int launch_w4_stream(StreamArgs a, cudaStream_t stream) {
+    if (a.P <= 0) return W4A8_OK;
+    a.ks_n = (a.G + kSpi - 1) / kSpi;
+    a.rg_n = (a.N + kRowsPerItem - 1) / kRowsPerItem;
+    // K splits and the SiLU epilogues (gate row n pairs with up row n + N/2, computed by other
+    // warps) go through the fp32 partials and the finish kernel.
+    const bool silu = a.mode == kStreamSilu || a.mode == kStreamSiluQuant;
+    a.force_part = (a.ks_n > 1 || silu) ? 1 : 0;
+    if (a.force_part && !a.part) return set_error("internal: stream path needs a partials buffer");
+    if (a.mode == kStreamSiluQuant && (a.N / 2) % 128 != 0)
+        return set_error("internal: SiLU-quant needs inter % 128 == 0");
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    w4_stream_kernel<<<sms * 2, kWarps * 32, 0, stream>>>(a);
+    if (int rc = launch_status()) return rc;
+    if (a.force_part) {
+        const size_t smem = a.mode == kStreamSiluQuant ? (size_t)(a.N / 2) * 2 : 0;
+        if (smem > 48 * 1024)
+            cudaFuncSetAttribute(w4_stream_finish_kernel,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        w4_stream_finish_kernel<<<a.P, 256, smem, stream>>>(a);
+        return launch_status();
+    }
+    return W4A8_OK;
+}
+
+}  // namespace w4a8

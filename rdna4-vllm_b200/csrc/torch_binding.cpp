@@ -65,7 +65,7 @@ at::Tensor mmq_fp8_gemm_forward(const at::Tensor& x, const at::Tensor& w_packed,
     }
     const c10::cuda::CUDAGuard guard(x.device());
     auto out = at::empty({M, N}, x.options());
-    auto ws = workspace(x, w4a8_mmq_fp8_gemm_workspace_size(M, K));
+    auto ws = workspace(x, w4a8_mmq_fp8_gemm_workspace_size(M, N, K));
     check_status(w4a8_mmq_fp8_gemm(x.data_ptr(), w_packed.data_ptr<int32_t>(), scales.data_ptr(),
                                    zeros_ptr(w_zeros), out.data_ptr(), M, N, K, group_size,
                                    (int32_t)kernel, weight_is_e2m1 ? 1 : 0, ws.data_ptr(),
@@ -146,7 +146,7 @@ at::Tensor mmq_fp8_moe_gemm_forward(const at::Tensor& x, const at::Tensor& w_pac
                                 sorted_token_ids, expert_ids, ntp, block_m, false);
     const c10::cuda::CUDAGuard guard(x.device());
     auto out = at::empty({d.P, d.N}, x.options());
-    auto ws = workspace(x, w4a8_moe_gemm_workspace_size(d.T, d.K));
+    auto ws = workspace(x, w4a8_moe_gemm_workspace_size(d.T, d.P, d.N, d.K));
     check_status(w4a8_mmq_fp8_moe_gemm(
                      x.data_ptr(), w_packed.data_ptr<int32_t>(), scales.data_ptr(),
                      zeros_ptr(w_zeros), sorted_token_ids.data_ptr<int32_t>(),
@@ -167,7 +167,7 @@ at::Tensor gemm1_silu_impl(const at::Tensor& x, const at::Tensor& w_packed,
     TORCH_CHECK(d.N % 2 == 0, "w13 N must be 2*inter (even); got ", d.N);
     const c10::cuda::CUDAGuard guard(x.device());
     auto out = at::empty({d.P, d.N / 2}, x.options());
-    auto ws = workspace(x, w4a8_moe_gemm_workspace_size(d.T, d.K));
+    auto ws = workspace(x, w4a8_moe_gemm_workspace_size(d.T, d.P, d.N, d.K));
     check_status(w4a8_mmq_fp8_moe_gemm1_silu(
                      x.data_ptr(), w_packed.data_ptr<int32_t>(), scales.data_ptr(),
                      zeros_ptr(w_zeros), sorted_token_ids.data_ptr<int32_t>(),
@@ -209,7 +209,7 @@ void mmq_fp8_moe_gemm_scatter_forward(const at::Tensor& x, const at::Tensor& w_p
     TORCH_CHECK(topk_weights.numel() == M * top_k, "topk_weights must have M*top_k=", M * top_k,
                 " entries");
     const c10::cuda::CUDAGuard guard(x.device());
-    auto ws = workspace(x, w4a8_moe_gemm_workspace_size(d.P, d.K));
+    auto ws = workspace(x, w4a8_moe_gemm_workspace_size(d.P, d.P, d.N, d.K));
     check_status(w4a8_mmq_fp8_moe_gemm_scatter(
                      x.data_ptr(), w_packed.data_ptr<int32_t>(), scales.data_ptr(),
                      zeros_ptr(w_zeros), sorted_token_ids.data_ptr<int32_t>(),

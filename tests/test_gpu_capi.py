@@ -25,11 +25,11 @@ def lib():
     L.w4a8_moe_align_block_size.argtypes = [c_vp, c_i64, c_i32, c_i32, c_i32, c_vp, c_vp, c_i64,
                                             c_vp, c_vp, c_vp, c_sz, c_vp]
     L.w4a8_mmq_fp8_gemm_workspace_size.restype = c_sz
-    L.w4a8_mmq_fp8_gemm_workspace_size.argtypes = [c_i64, c_i64]
+    L.w4a8_mmq_fp8_gemm_workspace_size.argtypes = [c_i64, c_i64, c_i64]
     L.w4a8_mmq_fp8_gemm.argtypes = [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64,
                                     c_i32, c_i32, c_vp, c_sz, c_vp]
     L.w4a8_moe_gemm_workspace_size.restype = c_sz
-    L.w4a8_moe_gemm_workspace_size.argtypes = [c_i64, c_i64]
+    L.w4a8_moe_gemm_workspace_size.argtypes = [c_i64, c_i64, c_i64, c_i64]
     L.w4a8_mmq_fp8_moe_gemm.argtypes = [c_vp] * 8 + [c_i64] * 8 + [c_i32, c_i32, c_vp, c_sz, c_vp]
     return L
 
@@ -84,7 +84,7 @@ def test_capi_dense_gemm(lib, kernel):
     x, c, s, z = I.dense_case(0, M, N, K, 128, True)
     xd, wd, sd, zd = cu(x), cu(O.pack_int4(c)), cu(s), cu(O.pack_zeros(z))
     out = torch.empty((M, N), dtype=torch.float16, device="cuda")
-    ws_n = lib.w4a8_mmq_fp8_gemm_workspace_size(M, K)
+    ws_n = lib.w4a8_mmq_fp8_gemm_workspace_size(M, N, K)
     ws = torch.empty(ws_n, dtype=torch.uint8, device="cuda")
     ok(lib, lib.w4a8_mmq_fp8_gemm(xd.data_ptr(), wd.data_ptr(), sd.data_ptr(), zd.data_ptr(),
                                   out.data_ptr(), M, N, K, 128, kernel, 0, ws.data_ptr(), ws_n,
@@ -105,7 +105,7 @@ def test_capi_moe_gemm_gemv(lib):
     bufs = [cu(x), cu(O.pack_int4(codes)), cu(scales), cu(O.pack_zeros(zeros)), cu(s), cu(e),
             cu(np.array([n], np.int32))]
     out = torch.empty((P, N), dtype=torch.float16, device="cuda")
-    ws_n = lib.w4a8_moe_gemm_workspace_size(T, K)
+    ws_n = lib.w4a8_moe_gemm_workspace_size(T, P, N, K)
     ws = torch.empty(ws_n, dtype=torch.uint8, device="cuda")
     ok(lib, lib.w4a8_mmq_fp8_moe_gemm(*[b.data_ptr() for b in bufs], out.data_ptr(), T, E, N, K,
                                       P, 128, k, bm, 7, 0, ws.data_ptr(), ws_n, stream()))

@@ -24,8 +24,8 @@ def test_version_and_workspace_queries():
     lib.w4a8_version.restype = ctypes.c_char_p
     assert b"sm_100a" in lib.w4a8_version()
     lib.w4a8_mmq_fp8_gemm_workspace_size.restype = c_sz
-    lib.w4a8_mmq_fp8_gemm_workspace_size.argtypes = [c_i64, c_i64]
-    assert lib.w4a8_mmq_fp8_gemm_workspace_size(16, 2048) >= 16 * 2048 + 16 * 4
+    lib.w4a8_mmq_fp8_gemm_workspace_size.argtypes = [c_i64, c_i64, c_i64]
+    assert lib.w4a8_mmq_fp8_gemm_workspace_size(16, 2048, 2048) >= 16 * 2048 * 3 + 16 * 4
     lib.w4a8_moe_align_workspace_size.restype = c_sz
     lib.w4a8_moe_align_workspace_size.argtypes = [c_i32]
     assert lib.w4a8_moe_align_workspace_size(256) >= 257 * 4
