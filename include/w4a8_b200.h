@@ -171,6 +171,26 @@ W4A8_API int w4a8_moe_gather_reduce(const void* out2, const int32_t* sorted_toke
                            float* out, int64_t M, int64_t N, int64_t P, int64_t top_k,
                            void* workspace, size_t workspace_bytes, w4a8_stream_t stream);
 
+/*
+ * Whole gated MoE layer at decode sizes in one call: moe_align (block 8) -> gate_up GEMV ->
+ * silu_and_mul -> down GEMV -> topk-weighted reduce, the decode branch of the reference's
+ * composition _run_grouped_moe (w4a8_fp8_wmma/w4a8_fp8_wmma/moe_experts.py:563-648), which
+ * there takes four ops plus vLLM's align and activation.
+ *   x (T, H) fp16; topk_ids (T, top_k) int32; topk_weights (T, top_k) fp32;
+ *   w13 (E, 2I, H/8) int32 [gate | up], s13 (E, 2I, H/128) fp16, z13 (E, 2I/8, H/128) or NULL;
+ *   w2 (E, H, I/8), s2 (E, H, I/128), z2 (E, H/8, I/128) or NULL;
+ *   out (T, H) fp16 = sum_j topk_weights[t, j] * fp16(down_j(silu_and_mul(gate_up_j(x_t)))).
+ * group_size must be 128 and H, I multiples of 512.
+ */
+W4A8_API size_t w4a8_moe_decode_workspace_size(int64_t T, int64_t top_k, int64_t E, int64_t H,
+                                               int64_t I);
+W4A8_API int w4a8_moe_decode(const void* x, const int32_t* topk_ids, const float* topk_weights,
+                             int64_t T, int64_t top_k, int64_t E, const int32_t* w13,
+                             const void* s13, const int32_t* z13, const int32_t* w2,
+                             const void* s2, const int32_t* z2, int64_t H, int64_t I,
+                             int64_t group_size, void* out, void* workspace,
+                             size_t workspace_bytes, w4a8_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -181,30 +181,36 @@ __device__ __forceinline__ void compute_item(const StreamArgs& a, const Smem& sm
                                              const ItemMeta& m, int buf, int warp, int lane,
                                              const WeightRegs& r) {
     const int c = lane & 3, tok = lane >> 2;
+    // item fields into registers once (the shared slot would be re-read after every MMA)
+    const int m_any = m.any, m_b = m.b, m_ks = m.ks, m_rg = m.rg;
     const int nl = warp * 16 + tok;              // local row (0..127) of the item
-    const int n0 = m.rg * kRowsPerItem + nl;
-    if (m.rg * kRowsPerItem + warp * 16 >= a.N) return;   // warp beyond N
+    const int n0 = m_rg * kRowsPerItem + nl;
+    if (m_rg * kRowsPerItem + warp * 16 >= a.N) return;   // warp beyond N
     float tot[4] = {0.f, 0.f, 0.f, 0.f};
-    if (!m.any) {
+    if (!m_any) {
         // all-padding block or non-local expert: rows are zeros for the direct store epilogue
         if (a.mode == kStreamStore && !a.force_part) {
             const int P_valid = a.ntp ? min(a.ntp[0], a.P) : a.P;
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) {
-                const int rr = m.b * 8 + 2 * c + (jj & 1), n = n0 + (jj >> 1) * 8;
+                const int rr = m_b * 8 + 2 * c + (jj & 1), n = n0 + (jj >> 1) * 8;
                 if (rr < P_valid && n < a.N) a.out16[(int64_t)rr * a.N + n] = __float2half_rn(0.f);
             }
         }
         return;
     }
+    const int src_c[2] = {m.src[2 * c], m.src[2 * c + 1]};
+    const int sid_c[2] = {m.sid[2 * c], m.sid[2 * c + 1]};
     const uint8_t* rowp = &sm.act[buf][tok][0];
     const int sh0 = (n0 & 7) * 4, sh1 = ((n0 + 8) & 7) * 4;
+    const int nj = min(kSpi, a.G - m_ks * kSpi);
 #pragma unroll
     for (int j = 0; j < kSpi; ++j) {
-        if (m.ks * kSpi + j >= a.G) break;
+        if (j >= nj) break;
         const uint32_t w0[4] = {r.w[j][0].x, r.w[j][0].y, r.w[j][0].z, r.w[j][0].w};
         const uint32_t w1[4] = {r.w[j][1].x, r.w[j][1].y, r.w[j][1].z, r.w[j][1].w};
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        // two independent accumulator chains (words 0,2 and 1,3) halve the MMA dependency depth
+        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             uint32_t h0[4], h1[4];
@@ -212,22 +218,24 @@ __device__ __forceinline__ void compute_item(const StreamArgs& a, const Smem& sm
             expand_word(w1[i], h1);
             const uint4 bq = *reinterpret_cast<const uint4*>(rowp + act_off(j, c, i));
             const uint32_t a0[4] = {h0[0], h1[0], h0[1], h1[1]};
-            mma_16816(acc, a0, bq.x, bq.y);
+            mma_16816(acc[i & 1], a0, bq.x, bq.y);
             const uint32_t a1[4] = {h0[2], h1[2], h0[3], h1[3]};
-            mma_16816(acc, a1, bq.z, bq.w);
+            mma_16816(acc[i & 1], a1, bq.z, bq.w);
         }
         float z0 = 8.f, z1 = 8.f;
         if (a.zeros) {
-            z0 = (float)((sm.zr[buf][nl >> 3][j] >> sh0) & 0xF);
-            z1 = (float)((sm.zr[buf][(nl + 8) >> 3][j] >> sh1) & 0xF);
+            // nibble -> float through the 2^23 magic (one LOP3 + one FADD, no conversion unit)
+            z0 = __uint_as_float(0x4B000000u | ((sm.zr[buf][nl >> 3][j] >> sh0) & 0xF)) - 8388608.f;
+            z1 = __uint_as_float(0x4B000000u | ((sm.zr[buf][(nl + 8) >> 3][j] >> sh1) & 0xF)) -
+                 8388608.f;
         }
         const float4 xs = *reinterpret_cast<const float4*>(&sm.xs[buf][j][2 * c]);  // K0,S x 2 cols
         const float s0 = __half2float(sm.sc[buf][nl][j]);
         const float s1 = __half2float(sm.sc[buf][nl + 8][j]);
-        tot[0] = fmaf(s0, fmaf(-z0, xs.y, acc[0] - xs.x), tot[0]);
-        tot[1] = fmaf(s0, fmaf(-z0, xs.w, acc[1] - xs.z), tot[1]);
-        tot[2] = fmaf(s1, fmaf(-z1, xs.y, acc[2] - xs.x), tot[2]);
-        tot[3] = fmaf(s1, fmaf(-z1, xs.w, acc[3] - xs.z), tot[3]);
+        tot[0] = fmaf(s0, fmaf(-z0, xs.y, (acc[0][0] + acc[1][0]) - xs.x), tot[0]);
+        tot[1] = fmaf(s0, fmaf(-z0, xs.w, (acc[0][1] + acc[1][1]) - xs.z), tot[1]);
+        tot[2] = fmaf(s1, fmaf(-z1, xs.y, (acc[0][2] + acc[1][2]) - xs.x), tot[2]);
+        tot[3] = fmaf(s1, fmaf(-z1, xs.w, (acc[0][3] + acc[1][3]) - xs.z), tot[3]);
     }
     // tot[0..1]: row n0, token columns 2c, 2c+1; tot[2..3]: row n0 + 8.
 #pragma unroll
@@ -235,13 +243,13 @@ __device__ __forceinline__ void compute_item(const StreamArgs& a, const Smem& sm
         const int col = 2 * c + (jj & 1);
         const int n = n0 + (jj >> 1) * 8;
         if (n >= a.N) continue;
-        const int src = m.src[col];
-        const int rr = m.b * 8 + col;
+        const int src = src_c[jj & 1];
+        const int rr = m_b * 8 + col;
         if (a.force_part) {
-            if (src >= 0) a.part[((int64_t)m.ks * a.P + rr) * a.N + n] = tot[jj];
+            if (src >= 0) a.part[((int64_t)m_ks * a.P + rr) * a.N + n] = tot[jj];
         } else if (a.mode == kStreamScatter) {
             if (src >= 0) {
-                const int sid = m.sid[col];
+                const int sid = sid_c[jj & 1];
                 atomicAdd(a.out32 + (int64_t)(sid / a.out_top_k) * a.N + n,
                           a.topk_weights[sid] * tot[jj] * a.act_scales[src]);
             }

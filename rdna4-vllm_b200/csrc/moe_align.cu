@@ -82,7 +82,8 @@ template <bool kSmem>
 __global__ void __launch_bounds__(kPlaceWarps * 32)
 align_place_kernel(const int32_t* __restrict__ topk_ids, int64_t num_slots, int num_experts,
                    int num_local, const int32_t* __restrict__ expert_map,
-                   const int32_t* __restrict__ offsets, int32_t* __restrict__ sorted_ids) {
+                   const int32_t* __restrict__ offsets, int32_t* __restrict__ sorted_ids,
+                   int32_t* __restrict__ slot_to_row) {
     extern __shared__ int16_t ids[];
     if (kSmem) {
         for (int64_t i = threadIdx.x; i < num_slots; i += blockDim.x)
@@ -101,7 +102,11 @@ align_place_kernel(const int32_t* __restrict__ topk_ids, int64_t num_slots, int 
         int le = -1;
         if (i < num_slots) le = kSmem ? (int)ids[i] : local_expert(topk_ids, expert_map, i, num_experts);
         const uint32_t m = __ballot_sync(0xffffffffu, le == e);
-        if (le == e) sorted_ids[run + __popc(m & lt)] = (int32_t)i;
+        if (le == e) {
+            const int32_t pos = run + __popc(m & lt);
+            sorted_ids[pos] = (int32_t)i;
+            if (slot_to_row) slot_to_row[i] = pos;  // inverse map for the gather-reduce
+        }
         run += __popc(m);
     }
     const int32_t sentinel = (int32_t)num_slots;
@@ -116,14 +121,13 @@ extern "C" size_t w4a8_moe_align_workspace_size(int32_t num_local_experts) {
     return w4a8::align_up(((size_t)num_local_experts + 1) * sizeof(int32_t), 256);
 }
 
-extern "C" int w4a8_moe_align_block_size(const int32_t* topk_ids, int64_t num_slots,
-                                         int32_t num_experts, int32_t num_local_experts,
-                                         int32_t block_m, const int32_t* expert_map,
-                                         int32_t* sorted_token_ids, int64_t sorted_capacity,
-                                         int32_t* expert_ids, int32_t* num_tokens_post_padded,
-                                         void* workspace, size_t workspace_bytes,
-                                         w4a8_stream_t stream) {
-    using namespace w4a8;
+namespace w4a8 {
+
+int launch_moe_align(const int32_t* topk_ids, int64_t num_slots, int32_t num_experts,
+                     int32_t num_local_experts, int32_t block_m, const int32_t* expert_map,
+                     int32_t* sorted_token_ids, int64_t sorted_capacity, int32_t* expert_ids,
+                     int32_t* num_tokens_post_padded, void* workspace, size_t workspace_bytes,
+                     int32_t* slot_to_row, cudaStream_t stream) {
     if (num_slots < 0 || num_experts <= 0 || num_local_experts <= 0 || block_m <= 0)
         return set_error("moe_align: sizes must be positive");
     if (num_slots >= (int64_t)INT32_MAX) return set_error("moe_align: too many slots");
@@ -158,11 +162,26 @@ extern "C" int w4a8_moe_align_block_size(const int32_t* topk_ids, int64_t num_sl
                              (int)(kMaxSmemSlots * sizeof(int16_t)));
         align_place_kernel<true><<<grid, kPlaceWarps * 32, smem, stream>>>(
             topk_ids, num_slots, num_experts, num_local_experts, expert_map, offsets,
-            sorted_token_ids);
+            sorted_token_ids, slot_to_row);
     } else {
         align_place_kernel<false><<<grid, kPlaceWarps * 32, 0, stream>>>(
             topk_ids, num_slots, num_experts, num_local_experts, expert_map, offsets,
-            sorted_token_ids);
+            sorted_token_ids, slot_to_row);
     }
     return launch_status();
+}
+
+}  // namespace w4a8
+
+extern "C" int w4a8_moe_align_block_size(const int32_t* topk_ids, int64_t num_slots,
+                                         int32_t num_experts, int32_t num_local_experts,
+                                         int32_t block_m, const int32_t* expert_map,
+                                         int32_t* sorted_token_ids, int64_t sorted_capacity,
+                                         int32_t* expert_ids, int32_t* num_tokens_post_padded,
+                                         void* workspace, size_t workspace_bytes,
+                                         w4a8_stream_t stream) {
+    return w4a8::launch_moe_align(topk_ids, num_slots, num_experts, num_local_experts, block_m,
+                                  expert_map, sorted_token_ids, sorted_capacity, expert_ids,
+                                  num_tokens_post_padded, workspace, workspace_bytes, nullptr,
+                                  reinterpret_cast<cudaStream_t>(stream));
 }

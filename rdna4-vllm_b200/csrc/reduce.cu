@@ -22,9 +22,10 @@ __global__ void build_inverse_map_kernel(const int32_t* __restrict__ sorted_ids,
 }
 
 // One CTA per (token, 512-channel chunk); each thread reduces 2 adjacent channels.
+template <typename OutT>
 __global__ void __launch_bounds__(256)
 gather_reduce_kernel(const __half* __restrict__ out2, const int32_t* __restrict__ slot_to_row,
-                     const float* __restrict__ topk_w, float* __restrict__ out, int64_t N,
+                     const float* __restrict__ topk_w, OutT* __restrict__ out, int64_t N,
                      int top_k) {
     const int64_t t = blockIdx.y;
     const int64_t n = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 2;
@@ -45,11 +46,25 @@ gather_reduce_kernel(const __half* __restrict__ out2, const int32_t* __restrict_
             if (pair) a1 = __fadd_rn(a1, __fmul_rn(w, __half2float(rowp[1])));
         }
     }
-    out[t * N + n] = a0;
-    if (pair) out[t * N + n + 1] = a1;
+    out[t * N + n] = (OutT)a0;
+    if (pair) out[t * N + n + 1] = (OutT)a1;
 }
 
 }  // namespace
+
+int launch_gather_reduce(const __half* out2, const int32_t* slot_to_row, const float* topk_w,
+                         void* out, bool out_half, int64_t M, int64_t N, int top_k,
+                         cudaStream_t stream) {
+    if (M <= 0) return W4A8_OK;
+    const dim3 grid((unsigned)((N + 511) / 512), (unsigned)M);
+    if (out_half)
+        gather_reduce_kernel<__half><<<grid, 256, 0, stream>>>(out2, slot_to_row, topk_w,
+                                                               static_cast<__half*>(out), N, top_k);
+    else
+        gather_reduce_kernel<float><<<grid, 256, 0, stream>>>(out2, slot_to_row, topk_w,
+                                                              static_cast<float*>(out), N, top_k);
+    return launch_status();
+}
 
 }  // namespace w4a8
 
@@ -80,8 +95,6 @@ extern "C" int w4a8_moe_gather_reduce(const void* out2, const int32_t* sorted_to
             sorted_token_ids, num_tokens_post_padded, map, P, M * top_k);
         if (int rc = launch_status()) return rc;
     }
-    const dim3 grid((unsigned)((N + 511) / 512), (unsigned)M);
-    gather_reduce_kernel<<<grid, 256, 0, st>>>(static_cast<const __half*>(out2), map,
-                                               topk_weights, out, N, (int)top_k);
-    return launch_status();
+    return launch_gather_reduce(static_cast<const __half*>(out2), map, topk_weights, out, false, M,
+                                N, (int)top_k, st);
 }

@@ -295,6 +295,48 @@ std::vector<at::Tensor> moe_align_block_size_forward(const at::Tensor& topk_ids,
     return {sorted, eids, ntp};
 }
 
+at::Tensor moe_decode_forward(const at::Tensor& x, const at::Tensor& w13, const at::Tensor& s13,
+                              const at::Tensor& z13, const at::Tensor& w2, const at::Tensor& s2,
+                              const at::Tensor& z2, const at::Tensor& topk_weights,
+                              const at::Tensor& topk_ids) {
+    TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kHalf && x.dim() == 2 && x.is_contiguous(),
+                "x must be a contiguous (T, H) fp16 CUDA tensor");
+    TORCH_CHECK(w13.dim() == 3 && w2.dim() == 3 && w13.scalar_type() == at::kInt &&
+                    w2.scalar_type() == at::kInt && w13.is_contiguous() && w2.is_contiguous(),
+                "w13 (E, 2I, H/8) and w2 (E, H, I/8) must be contiguous int32");
+    TORCH_CHECK(s13.scalar_type() == at::kHalf && s2.scalar_type() == at::kHalf &&
+                    s13.is_contiguous() && s2.is_contiguous(),
+                "scales must be contiguous fp16");
+    TORCH_CHECK(topk_ids.scalar_type() == at::kInt && topk_weights.scalar_type() == at::kFloat &&
+                    topk_ids.is_contiguous() && topk_weights.is_contiguous() &&
+                    topk_ids.dim() == 2 && topk_weights.sizes() == topk_ids.sizes(),
+                "topk_ids (T, k) int32 and topk_weights (T, k) fp32 must be contiguous");
+    const int64_t T = x.size(0), H = x.size(1), E = w13.size(0), I = w13.size(1) / 2;
+    const int64_t k = topk_ids.size(1);
+    TORCH_CHECK(topk_ids.size(0) == T, "topk_ids must have T rows");
+    TORCH_CHECK(w13.size(2) * 8 == H && w2.size(0) == E && w2.size(1) == H && w2.size(2) * 8 == I,
+                "weight shapes do not match x");
+    TORCH_CHECK(s13.numel() == E * 2 * I * (H / 128) && s2.numel() == E * H * (I / 128),
+                "scales must be (E, N, K/128)");
+    const bool zz = z13.defined() && z13.numel() > 0;
+    TORCH_CHECK(zz == (z2.defined() && z2.numel() > 0), "give both zero tensors or neither");
+    if (zz)
+        TORCH_CHECK(z13.numel() == E * (2 * I / 8) * (H / 128) && z2.numel() == E * (H / 8) * (I / 128) &&
+                        z13.is_contiguous() && z2.is_contiguous(),
+                    "zeros must be (E, N/8, K/128) int32");
+    const c10::cuda::CUDAGuard guard(x.device());
+    auto out = at::empty({T, H}, x.options());
+    auto ws = workspace(x, w4a8_moe_decode_workspace_size(T, k, E, H, I));
+    check_status(w4a8_moe_decode(x.data_ptr(), topk_ids.data_ptr<int32_t>(),
+                                 topk_weights.data_ptr<float>(), T, k, E,
+                                 w13.data_ptr<int32_t>(), s13.data_ptr(), zz ? z13.data_ptr<int32_t>() : nullptr,
+                                 w2.data_ptr<int32_t>(), s2.data_ptr(), zz ? z2.data_ptr<int32_t>() : nullptr,
+                                 H, I, 128, out.data_ptr(), ws.data_ptr(), (size_t)ws.numel(),
+                                 cur_stream()),
+                 "moe_decode");
+    return out;
+}
+
 }  // namespace
 
 // pt2_compliant_tag on every op, as the reference registers them (bindings.cpp:388-413); the
@@ -339,6 +381,9 @@ TORCH_LIBRARY_IMPL(w4a8_fp8_wmma, CUDA, m) {
 
 TORCH_LIBRARY(w4a8_b200, m) {
     m.def("act_quant_fp8(Tensor x) -> Tensor[]");
+    // Whole gated MoE layer at decode sizes (align -> gate_up+SiLU -> down -> reduce).
+    m.def("moe_decode(Tensor x, Tensor w13, Tensor s13, Tensor z13, Tensor w2, Tensor s2, "
+          "Tensor z2, Tensor topk_weights, Tensor topk_ids) -> Tensor");
     // Fused gate_up + SiLU with any MoE kernel id (0 scalar, 6 tile, 7 GEMV).
     m.def("moe_gemm1_silu(Tensor x, Tensor w_packed, Tensor scales, Tensor w_zeros, "
           "Tensor sorted_token_ids, Tensor expert_ids, Tensor num_tokens_post_padded, "
@@ -349,6 +394,7 @@ TORCH_LIBRARY(w4a8_b200, m) {
 
 TORCH_LIBRARY_IMPL(w4a8_b200, CUDA, m) {
     m.impl("act_quant_fp8", &act_quant_fp8_forward);
+    m.impl("moe_decode", &moe_decode_forward);
     m.impl("moe_gemm1_silu", &gemm1_silu_impl);
     m.impl("moe_align_block_size", &moe_align_block_size_forward);
 }

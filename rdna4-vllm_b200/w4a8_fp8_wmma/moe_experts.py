@@ -64,6 +64,15 @@ def run_grouped_moe(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, w1_s: t
                                          global_num_experts, expert_map, False, out_dtype)
         return out
     use_gemv = kernel != "scalar" and M <= GEMV_MAX_M
+    if (use_gemv and expert_map is None and not apply_router_weight_on_input
+            and _fused_decode_ok(x, w1, w2, w1_s, w2_s, w1_zp, w2_zp, E_global)):
+        # whole layer in one op: align -> gate_up+SiLU -> down -> reduce (7 launches)
+        z1 = w1_zp if w1_zp is not None else torch.empty(0, dtype=torch.int32, device=dev)
+        z2 = w2_zp if w2_zp is not None else torch.empty(0, dtype=torch.int32, device=dev)
+        y = torch.ops.w4a8_b200.moe_decode(
+            x.contiguous(), w1, w1_s.contiguous(), z1, w2, w2_s.contiguous(), z2,
+            topk_weights.to(torch.float32).contiguous(), topk_ids.to(torch.int32).contiguous())
+        return y if out_dtype == torch.float16 else y.to(out_dtype)
     block_m = GEMV_BLOCK_M if use_gemv else TILE_BLOCK_M
     gver = "gemv" if use_gemv else kernel
     sorted_ids, expert_ids, ntp = moe_align_block_size(
@@ -90,6 +99,18 @@ def run_grouped_moe(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, w1_s: t
                             w_zeros=w2_zp)
     acc = mmq_fp8_moe_gather_reduce(out2, sorted_ids, tw, ntp, top_k)
     return acc.to(out_dtype)
+
+
+def _fused_decode_ok(x, w1, w2, w1_s, w2_s, w1_zp, w2_zp, E_global) -> bool:
+    """The fused decode op serves fp16 activations, g128 scales and hidden/inter % 512 == 0."""
+    if x.dtype != torch.float16 or w1.size(0) != E_global:
+        return False
+    H, I = x.size(1), w1.size(1) // 2
+    if H % 512 or I % 512 or w1_s.dtype != torch.float16 or w2_s.dtype != torch.float16:
+        return False
+    if w1_s.size(2) * 128 != H or w2_s.size(2) * 128 != I:
+        return False
+    return (w1_zp is None) == (w2_zp is None)
 
 
 # --------------------------------------------------------------------------------------------

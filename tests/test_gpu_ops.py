@@ -301,3 +301,20 @@ def test_silu_op_requires_wmma(w4):
     i32 = torch.zeros(16, dtype=torch.int32, device="cuda")
     with pytest.raises(RuntimeError, match="needs the 'wmma' kernel"):
         w4.mmq_fp8_moe_gemm1_silu(x, w, s, i32, i32[:2], i32[:1], 2, 8, kernel="gemv")
+
+
+@pytest.mark.parametrize("T,E,asym", [(1, 64, True), (32, 257, True), (32, 64, False),
+                                      (96, 64, True)])
+def test_fused_decode_layer_vs_oracle(w4, T, E, asym):
+    """torch.ops.w4a8_b200.moe_decode (the one-call decode layer) against the oracle layer."""
+    c = I.moe_layer_case(700 + T + E, T, E, 2048, 512, 8, 128, asym=asym)
+    z1 = cu(O.pack_zeros(c["z13"])) if asym else torch.empty(0, dtype=torch.int32, device="cuda")
+    z2 = cu(O.pack_zeros(c["z2"])) if asym else torch.empty(0, dtype=torch.int32, device="cuda")
+    y = torch.ops.w4a8_b200.moe_decode(cu(c["x"]), cu(O.pack_int4(c["c13"])), cu(c["s13"]), z1,
+                                       cu(O.pack_int4(c["c2"])), cu(c["s2"]), z2,
+                                       cu(c["topk_weights"]), cu(c["topk_ids"]))
+    ref = O.moe_layer(c["x"], O.pack_int4(c["c13"]), c["s13"],
+                      O.pack_zeros(c["z13"]) if asym else None, O.pack_int4(c["c2"]), c["s2"],
+                      O.pack_zeros(c["z2"]) if asym else None, c["topk_ids"], c["topk_weights"])
+    assert y.dtype == torch.float16
+    assert max_abs_rel(y.float().cpu().numpy(), ref) <= MAX_ABS_REL
