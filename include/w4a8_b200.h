@@ -94,6 +94,25 @@ W4A8_API int w4a8_moe_align_block_size(const int32_t* topk_ids, int64_t num_slot
                               size_t workspace_bytes, w4a8_stream_t stream);
 
 /*
+ * moe_align_block_size without a workspace argument, for callers that cannot allocate device
+ * memory when they route (a framework's private memory pool, a binding with no allocator, a
+ * deployment that bans cudaMalloc after start-up). No counterpart in the reference: its align
+ * comes from vLLM. The per-expert offsets live in a fixed 16 KB device array inside the
+ * library, so num_local_experts is limited to 4095 (larger values return W4A8_ERR_INVALID).
+ * The first call on each device looks the array's address up (cudaGetSymbolAddress) with that
+ * device current; make that first call before any stream capture. The array is shared by all
+ * calls on a device: calls that overlap on the GPU (different streams, no ordering) race.
+ * Arguments and results are those of w4a8_moe_align_block_size.
+ */
+W4A8_API int w4a8_moe_align_block_size_noalloc(const int32_t* topk_ids, int64_t num_slots,
+                                               int32_t num_experts, int32_t num_local_experts,
+                                               int32_t block_m, const int32_t* expert_map,
+                                               int32_t* sorted_token_ids,
+                                               int64_t sorted_capacity, int32_t* expert_ids,
+                                               int32_t* num_tokens_post_padded,
+                                               w4a8_stream_t stream);
+
+/*
  * Dense W4A8 GEMM: out (M, N) fp16 = x (M, K) fp16 @ dequant(w)^T.
  * Replaces launch_mmq_fp8_gemm_gfx1201 (w4a8_fp8_wmma/w4a8_fp8_wmma_kernel.hip:2507-2994) behind
  * the op mmq_fp8_gemm (bindings.cpp:98-146). kernel: 0 scalar golden, 5/10 tile path, 11 decode

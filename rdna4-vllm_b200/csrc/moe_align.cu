@@ -185,3 +185,68 @@ extern "C" int w4a8_moe_align_block_size(const int32_t* topk_ids, int64_t num_sl
                                   num_tokens_post_padded, workspace, workspace_bytes, nullptr,
                                   reinterpret_cast<cudaStream_t>(stream));
 }
+
+// ---------------------------------------------------------------------------------------------
+// Allocation-free variant of moe_align_block_size.
+//
+// Some callers cannot allocate device memory at the point where they route tokens: code that
+// runs inside another framework's memory pool without a handle to it, plugins whose host
+// language binding exposes no allocator, or deployments that forbid cudaMalloc after start-up
+// because it synchronises the device. For them the per-expert offsets that the ordinary entry
+// point keeps in caller workspace live in this fixed device array instead. It holds up to
+// kNoAllocMaxExperts + 1 offsets (16 KB); every GPU that loads the library keeps it until the
+// process exits.
+// ---------------------------------------------------------------------------------------------
+#include <mutex>
+
+namespace {
+
+constexpr int32_t kNoAllocMaxExperts = 4095;
+static __device__ __align__(256) int32_t g_align_noalloc_scratch[kNoAllocMaxExperts + 1];
+
+// Device address of the array, looked up once per device with that device current. The name
+// g_align_noalloc_scratch is only a host-side stand-in in host code; kernels must get this
+// address instead.
+int noalloc_scratch(void** out) {
+    constexpr int kMaxDevices = 64;
+    static std::mutex mu;
+    static void* addr[kMaxDevices] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= kMaxDevices) return w4a8::set_error("moe_align_noalloc: device index out of range");
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_align_noalloc_scratch);
+        if (e != cudaSuccess) return (int)e;
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return W4A8_OK;
+}
+
+}  // namespace
+
+extern "C" int w4a8_moe_align_block_size_noalloc(const int32_t* topk_ids, int64_t num_slots,
+                                                 int32_t num_experts, int32_t num_local_experts,
+                                                 int32_t block_m, const int32_t* expert_map,
+                                                 int32_t* sorted_token_ids,
+                                                 int64_t sorted_capacity, int32_t* expert_ids,
+                                                 int32_t* num_tokens_post_padded,
+                                                 w4a8_stream_t stream) {
+    if (num_local_experts > kNoAllocMaxExperts)
+        return w4a8::set_error("moe_align_noalloc: at most " +
+                               std::to_string(kNoAllocMaxExperts) +
+                               " local experts (fixed device scratch); got " +
+                               std::to_string(num_local_experts));
+    void* scratch = nullptr;
+    if (int rc = noalloc_scratch(&scratch)) return rc;
+    // The count kernel writes every offset it uses before the place kernel reads it, so the
+    // array needs no clearing between calls.
+    return w4a8::launch_moe_align(topk_ids, num_slots, num_experts, num_local_experts, block_m,
+                                  expert_map, sorted_token_ids, sorted_capacity, expert_ids,
+                                  num_tokens_post_padded, scratch,
+                                  sizeof(int32_t) * (kNoAllocMaxExperts + 1), nullptr,
+                                  reinterpret_cast<cudaStream_t>(stream));
+}
