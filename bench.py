@@ -141,7 +141,7 @@ def make_tokens(T: int, zipf: bool, seed: int):
 def run_ours(args):
     import torch
     import torch.distributed as dist
-    import w4a8_fp8_wmma as w4
+    import w4a8_fp8_wmma as w4  # noqa: F401  (loads the native libraries)
     from w4a8_fp8_wmma.moe_experts import run_grouped_moe
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -154,27 +154,39 @@ def run_ours(args):
     cfg = workload_config(args.workload)
     T = cfg["T"]
     E_total = E_ROUTED + 1
+    x_np, ids_np, w_np = make_tokens(T, cfg["zipf"], cfg["seed"] * 1000 + rank)
+    x = torch.from_numpy(x_np).to(dev)
+    ids = torch.from_numpy(ids_np).to(dev)
+    tw = torch.from_numpy(w_np).to(dev)
+    holder = {}
     if world > 1:
         from w4a8_fp8_wmma.ep import ExpertParallelMoE
-        layer = ExpertParallelMoE.synthetic(E_ROUTED, H, INTER, GROUP, TOP_K, seed=1000, dev=dev)
-        x_np, ids_np, w_np = make_tokens(T, cfg["zipf"], cfg["seed"] * 1000 + rank)
-        step_fn, out_holder, inputs = layer.make_step(x_np, ids_np[:, :TOP_K], w_np[:, :TOP_K], T)
-        touched_bytes = layer.local_bytes()
-    else:
-        w13, s13, z13, w2, s2, z2 = make_layer(torch, dev, 1000, E_total)
-        x_np, ids_np, w_np = make_tokens(T, cfg["zipf"], cfg["seed"])
-        x = torch.from_numpy(x_np).to(dev)
-        ids = torch.from_numpy(ids_np).to(dev)
-        tw = torch.from_numpy(w_np).to(dev)
-        touched = np.unique(ids_np)
-        touched_bytes = len(touched) * EXPERT_BYTES
-        out_holder = {}
+        E_loc = E_ROUTED // world
+        wts = make_layer(torch, dev, 1000 + rank, E_loc)
+        shared = make_layer(torch, dev, 999, 1)
+        w13, s13, z13, w2, s2, z2 = wts
+        layer = ExpertParallelMoE(w13, s13, z13, w2, s2, z2, E_ROUTED, TOP_K, shared=shared)
+        ids_r = ids[:, :TOP_K].contiguous()
+        tw_r = tw[:, :TOP_K].contiguous()
+        recorded = {}
+        base_fn = layer.expert_fn
+
+        def recording_fn(rows, lid):
+            recorded["rows"], recorded["ids"] = rows, lid
+            return base_fn(rows, lid)
+        layer.expert_fn = recording_fn
 
         def step_fn():
-            out_holder["y"] = run_grouped_moe(x, w13, w2, s13, s2, z13, z2, tw, ids,
-                                              global_num_experts=E_total, out_dtype=torch.float16)
+            holder["y"] = layer(x, ids_r, tw_r)
+    else:
+        layer = None
+        w13, s13, z13, w2, s2, z2 = make_layer(torch, dev, 1000, E_total)
 
-    # CUDA graph of one step.
+        def step_fn():
+            holder["y"] = run_grouped_moe(x, w13, w2, s13, s2, z13, z2, tw, ids,
+                                          global_num_experts=E_total, out_dtype=torch.float16)
+
+    # One CUDA graph per step (NCCL collectives included); eager replay if capture fails.
     stream = torch.cuda.Stream()
     stream.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(stream):
@@ -182,11 +194,19 @@ def run_ours(args):
             step_fn()
     torch.cuda.current_stream().wait_stream(stream)
     torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        step_fn()
+    graph = None
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step_fn()
+        graph = g
+    except Exception as exc:  # noqa: BLE001
+        print(f"[bench] graph capture failed ({type(exc).__name__}); timing eager steps",
+              file=sys.stderr)
+        torch.cuda.synchronize()
+    run = graph.replay if graph is not None else step_fn
     for _ in range(args.warmup):
-        graph.replay()
+        run()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -196,31 +216,30 @@ def run_ours(args):
         torch.cuda.synchronize()
         start.record(replay_stream)
         for _ in range(args.steps):
-            graph.replay()
+            run()
         end.record(replay_stream)
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    ms = start.elapsed_time(end) / args.steps
-    t = torch.tensor([ms], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+    ms = _max_over_ranks(torch, dist, world, dev, start.elapsed_time(end) / args.steps)
     tokens_per_s = T * world / (ms / 1e3)
 
-    # Dominant kernel: time the gate_up grouped GEMM alone (same inputs) with CUDA events.
-    dom = dominant_kernel(torch, w4, args, world, layer if world > 1 else None,
-                          locals().get("x"), locals().get("ids"), locals().get("w13"),
-                          locals().get("s13"), locals().get("z13"), E_total, T)
-
-    # End to end through the public API: pinned host inputs -> device -> layer -> host output.
-    e2e = end_to_end(torch, args, world, locals())
+    # HBM bytes of the layer on this rank (max over ranks for the report).
+    if world > 1:
+        rec_ids = recorded["ids"]
+        touched = int(torch.unique(rec_ids[rec_ids >= 0]).numel()) + 1  # + shared expert
+    else:
+        touched = len(np.unique(ids_np))
+    touched_bytes = touched * EXPERT_BYTES
     hbm, fp8_peak, src = peaks()
     layer_bytes = touched_bytes + T * H * 2 * 2 + T * (TOP_K + 1) * 8
     flops = 2.0 * T * (TOP_K + 1) * (H * 2 * INTER + INTER * H)
+    dom = dominant_kernel(torch, args, world, dist, dev, x, ids, w13, s13, z13, E_total, T,
+                          recorded if world > 1 else None, layer)
+    e2e = end_to_end(torch, dist, args, world, dev, x_np, ids_np, w_np, layer, run_grouped_moe,
+                     (w13, s13, z13, w2, s2, z2), E_total)
     if rank != 0:
-        if world > 1:
-            dist.destroy_process_group()
+        dist.destroy_process_group()
         return
     res = {
         "metric": "MoE-layer tokens/s (Qwen3.6-35B-A3B-shaped, decode T=32)"
@@ -233,11 +252,13 @@ def run_ours(args):
                    "tokens_per_gpu": T, "hidden": H, "inter": INTER, "experts": E_ROUTED,
                    "shared_experts": 1, "top_k": TOP_K, "group": GROUP,
                    "parallelism": f"ep{world}" if world > 1 else "single",
-                   "l2": "touched weights > 126 MB L2 (no flush)",
+                   "l2": "touched weights > 126 MB L2 (no flush)" if world == 1 else
+                         "per-rank weights ~53-105 MB; inputs re-read each step",
+                   "rank0_hbm_bytes_per_step": layer_bytes,
                    "layer_hbm_gbs": round(layer_bytes / (ms / 1e3) / 1e9, 1),
                    "layer_hbm_frac_of_measured": round(layer_bytes / (ms / 1e3) / 1e9 / hbm, 4),
                    "layer_tflops": round(flops / (ms / 1e3) / 1e12, 2),
-                   "graph": "one CUDA graph per step"},
+                   "graph": "one CUDA graph per step" if graph is not None else "eager steps"},
         "roofline": dom,
         "clocks": clk.summary(),
         "e2e": e2e,
@@ -250,81 +271,107 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def launches_per_step(workload: str, world: int) -> int:
-    # align (2) + act-quant + gate_up/SiLU + act-quant + down + [gather-reduce: memset-free map
-    # build + reduce at prefill]
-    n = 6 if workload == "decode" else 8
+def _max_over_ranks(torch, dist, world, dev, v):
+    t = torch.tensor([float(v)], device=dev)
     if world > 1:
-        n += 4  # dispatch pack / unpack, combine pack / unpack
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def launches_per_step(workload: str, world: int) -> int:
+    """Kernels of this library per step: decode = align count + place, operand quant, gate_up
+    GEMV + finish, down GEMV, gather-reduce (7); prefill adds the tile-path act-quant launches.
+    EP adds the shared expert's 7 and the combine gather-reduce."""
+    n = 7 if workload == "decode" else 9
+    if world > 1:
+        n += 8
     return n
 
 
-def dominant_kernel(torch, w4, args, world, layer, x, ids, w13, s13, z13, E_total, T):
-    hbm, _, src = peaks()
-    if world > 1:
-        return layer.dominant_kernel_roofline(hbm, src)
-    block_m = 8 if T <= 96 else 64
-    kern = 7 if T <= 96 else 6
-    s, e, n = w4.moe_align_block_size(ids, block_m, E_total)
-    zero = torch.empty(0, dtype=torch.int32, device=x.device)
-    def launch():
-        return torch.ops.w4a8_b200.moe_gemm1_silu(x, w13, s13, z13, s, e, n, ids.size(1), block_m,
-                                                  kern, False)
+def _event_time(torch, fn, reps=20):
     for _ in range(3):
-        launch()
+        fn()
     torch.cuda.synchronize()
     st = torch.cuda.current_stream()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 20
     a.record(st)
     for _ in range(reps):
-        launch()
+        fn()
     b.record(st)
     torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / reps  # includes the act-quant launch of x (tiny)
-    touched = torch.unique(ids).numel()
-    bytes_ = touched * W13_BYTES + T * H + T * 4 + int(n.item()) * INTER * 2
-    ach = bytes_ / (ms / 1e3) / 1e9
-    return {"kernel": "w4_mma_kernel<gate_up+SiLU> (+act_quant)", "bound": "hbm",
-            "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s", "frac": round(ach / hbm, 4),
-            "peak_source": src, "algorithmic_bytes_per_launch": bytes_,
-            "avg_launch_us": round(ms * 1e3, 2), "traffic": None}
+    return a.elapsed_time(b) / reps
 
 
-def end_to_end(torch, args, world, env):
-    """Same metric through the public API with host buffers (pinned), copies inside timing."""
-    from w4a8_fp8_wmma.moe_experts import run_grouped_moe
+def dominant_kernel(torch, args, world, dist, dev, x, ids, w13, s13, z13, E_total, T, recorded,
+                    layer):
+    """The gate_up grouped GEMV op (operand quant + streaming GEMV + SiLU finish) on this
+    rank's rows, timed alone with CUDA events; algorithmic bytes = touched experts' w13 bytes
+    (codes + scales + zeros) + the fp16 activations read + the fp16 SiLU rows written."""
+    hbm, _, src = peaks()
+    import w4a8_fp8_wmma as w4
     if world > 1:
-        return env["layer"].end_to_end(args.steps, env["x_np"], env["ids_np"], env["w_np"])
-    x_h = torch.from_numpy(env["x_np"]).pin_memory()
-    ids_h = torch.from_numpy(env["ids_np"]).pin_memory()
-    w_h = torch.from_numpy(env["w_np"]).pin_memory()
-    dev = env["x"].device
-    w13, w2, s13, s2, z13, z2 = (env[k] for k in ("w13", "w2", "s13", "s2", "z13", "z2"))
-    out_h = torch.empty((env["T"], H), dtype=torch.float16).pin_memory()
+        xr = recorded["rows"]
+        idr = recorded["ids"].view(-1, 1).to(torch.int32)
+        idr = torch.where(idr >= 0, idr, torch.full_like(idr, w13.size(0)))
+        E_use, xx, ii = w13.size(0), xr, idr
+    else:
+        E_use, xx, ii = E_total, x, ids
+    block_m = 8 if xx.size(0) <= 96 or world > 1 else 64
+    kern = 7 if block_m == 8 else 6
+    s, e, n = w4.moe_align_block_size(ii, block_m, E_use)
+
+    def launch():
+        return torch.ops.w4a8_b200.moe_gemm1_silu(xx, w13, s13, z13, s, e, n, ii.size(1),
+                                                  block_m, kern, False)
+    ms = _max_over_ranks(torch, dist, world, dev, _event_time(torch, launch))
+    valid = ii[(ii >= 0) & (ii < E_use)]
+    touched = int(torch.unique(valid).numel())
+    rows = int(valid.numel())
+    bytes_ = touched * W13_BYTES + rows * H * 2 + rows * INTER * 2
+    ach = bytes_ / (ms / 1e3) / 1e9
+    return {"kernel": "gate_up grouped GEMV op: operand_quant + w4_stream_kernel + finish(SiLU)",
+            "bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+            "frac": round(ach / hbm, 4), "peak_source": src,
+            "algorithmic_bytes_per_launch": bytes_, "avg_launch_us": round(ms * 1e3, 2),
+            "traffic": STREAM_KERNEL_TRAFFIC if world == 1 else None,
+            "traffic_source": "profiles/w4_stream_kernel_decode.md (dram read+write, one ncu "
+                              "capture of the stream kernel)" if world == 1 else None}
+
+
+# dram__bytes_read.sum + dram__bytes_write.sum of the gate_up w4_stream_kernel launch in the
+# committed ncu capture (profiles/w4_stream_kernel_decode.md).
+STREAM_KERNEL_TRAFFIC = 185_420_544 + 4_915_968
+
+
+def end_to_end(torch, dist, args, world, dev, x_np, ids_np, w_np, layer, run_grouped_moe,
+               wts, E_total):
+    """Same metric through the public API with host buffers: pinned host inputs are copied in,
+    the layer runs (eager), the fp16 output is copied back, all inside the timed region."""
+    x_h = torch.from_numpy(x_np).pin_memory()
+    ids_h = torch.from_numpy(ids_np).pin_memory()
+    w_h = torch.from_numpy(w_np).pin_memory()
+    T = x_np.shape[0]
+    out_h = torch.empty((T, H), dtype=torch.float16).pin_memory()
+    w13, s13, z13, w2, s2, z2 = wts
+
     def once():
         x = x_h.to(dev, non_blocking=True)
         ids = ids_h.to(dev, non_blocking=True)
         tw = w_h.to(dev, non_blocking=True)
-        y = run_grouped_moe(x, w13, w2, s13, s2, z13, z2, tw, ids,
-                            global_num_experts=env["E_total"], out_dtype=torch.float16)
+        if world > 1:
+            y = layer(x, ids[:, :TOP_K].contiguous(), tw[:, :TOP_K].contiguous())
+        else:
+            y = run_grouped_moe(x, w13, w2, s13, s2, z13, z2, tw, ids,
+                                global_num_experts=E_total, out_dtype=torch.float16)
         out_h.copy_(y, non_blocking=True)
-    for _ in range(3):
-        once()
-    torch.cuda.synchronize()
-    st = torch.cuda.current_stream()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(st)
-    for _ in range(args.steps):
-        once()
-    b.record(st)
-    torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / args.steps
-    T = env["T"]
-    return {"value": round(T / (ms / 1e3), 1), "unit": "tokens/s",
+    if world > 1:
+        dist.barrier()
+    ms = _max_over_ranks(torch, dist, world, dev, _event_time(torch, once, reps=args.steps))
+    return {"value": round(T * world / (ms / 1e3), 1), "unit": "tokens/s",
             "h2d_bytes_per_step": int(x_h.numel() * 2 + ids_h.numel() * 4 + w_h.numel() * 4),
             "d2h_bytes_per_step": int(out_h.numel() * 2), "ms_per_step": round(ms, 4),
-            "path": "w4a8_fp8_wmma.moe_experts.run_grouped_moe (eager, no graph)"}
+            "path": "w4a8_fp8_wmma.moe_experts.run_grouped_moe" if world == 1 else
+                    "w4a8_fp8_wmma.ep.ExpertParallelMoE", "graph": "eager"}
 
 
 # ------------------------------------------------------------------------------------------

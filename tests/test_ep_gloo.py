@@ -1,0 +1,137 @@
+"""Expert-parallel dispatch/combine on CPU `gloo` ranks (world size 2), with an identity
+"expert" so the permutation logic is checked exactly; plus host-side failure cases: a rank
+that dies before the exchange and a rank holding the wrong expert shard raise instead of hang.
+"""
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from w4a8_fp8_wmma.ep import ExpertParallelMoE, plan_dispatch
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _init(rank, world, port, timeout_s=20):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    from datetime import timedelta
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=timeout_s))
+
+
+def _worker_identity(rank, world, port, q):
+    try:
+        _init(rank, world, port)
+        ok_all, count_all = True, True
+        for skew in (False, True):
+            torch.manual_seed(100 + rank)
+            T, H, E, k = 6, 16, 8, 3
+            x = torch.randn(T, H).to(torch.float16)
+            if skew:  # every slot routes to rank 0's experts
+                ids = torch.stack([torch.randperm(E // world)[:k] for _ in range(T)]).to(torch.int32)
+            else:
+                ids = torch.stack([torch.randperm(E)[:k] for _ in range(T)]).to(torch.int32)
+            w = torch.rand(T, k)
+            seen = []
+
+            def identity(rows, local_ids):
+                seen.append(int((local_ids >= 0).sum()))
+                assert torch.all(local_ids < E // world)
+                return rows  # the "expert" returns its input row
+
+            layer = ExpertParallelMoE(None, None, None, None, None, None, E, k, expert_fn=identity)
+            out = layer(x, ids, w)
+            ref = w.sum(1, keepdim=True) * x.to(torch.float32)
+            ok_all &= bool(torch.allclose(out, ref, rtol=1e-3, atol=1e-3))
+            # every slot is computed exactly once somewhere
+            tot = torch.tensor([seen[0]])
+            dist.all_reduce(tot)
+            count_all &= int(tot.item()) == T * k * world
+        q.put((rank, ok_all, count_all, None))
+        dist.destroy_process_group()
+    except Exception:
+        q.put((rank, False, False, traceback.format_exc()))
+
+
+def _spawn(fn, world, *args, reporters=None):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=fn, args=(r, world, port, q) + args) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(reporters or world)]
+    for p in procs:
+        p.join(timeout=60)
+    return sorted(res, key=lambda r: r[0])
+
+
+def test_ep_dispatch_combine_identity_world2():
+    res = _spawn(_worker_identity, 2)
+    for rank, ok, count_ok, err in res:
+        assert err is None, err
+        assert ok and count_ok, (rank, ok, count_ok)
+
+
+def test_plan_dispatch_positions_are_stable_and_dense():
+    ids = torch.tensor([[0, 5], [4, 1], [7, 2]], dtype=torch.int32)  # E=8, 2 ranks -> 4 per rank
+    dest, pos, row = plan_dispatch(ids, 4, 2, capacity=6)
+    assert dest.tolist() == [0, 1, 1, 0, 1, 0]
+    assert pos.tolist() == [0, 0, 1, 1, 2, 2]
+    assert row.tolist() == [0, 6, 7, 1, 8, 2]
+
+
+def _worker_dies(rank, world, port, q):
+    try:
+        _init(rank, world, port, timeout_s=10)
+        if rank == 1:
+            os._exit(0)  # leaves before the exchange without a word
+        layer = ExpertParallelMoE(None, None, None, None, None, None, 4, 1,
+                                  expert_fn=lambda r, i: r)
+        try:
+            layer(torch.zeros(2, 8, dtype=torch.float16), torch.tensor([[3], [2]], dtype=torch.int32),
+                  torch.ones(2, 1))
+            q.put((rank, False, False, "exchange with a dead peer returned"))
+        except Exception:  # expected: connection closed or timeout
+            q.put((rank, True, True, None))
+    except Exception:
+        q.put((rank, False, False, traceback.format_exc()))
+
+
+def test_dead_peer_raises_instead_of_hanging():
+    res = _spawn(_worker_dies, 2, reporters=1)  # only the surviving rank reports
+    for rank, ok, _, err in res:
+        assert err is None, err
+        assert ok, rank
+
+
+def _worker_bad_shard(rank, world, port, q):
+    try:
+        _init(rank, world, port)
+        w13 = torch.zeros(3 if rank == 1 else 4, 8, 2, dtype=torch.int32)
+        try:
+            ExpertParallelMoE(w13, None, None, None, None, None, 8, 2)
+            q.put((rank, rank == 0, True, None if rank == 0 else "bad shard accepted"))
+        except ValueError:
+            q.put((rank, rank == 1, True, None))
+        dist.destroy_process_group()
+    except Exception:
+        q.put((rank, False, False, traceback.format_exc()))
+
+
+def test_wrong_expert_shard_rejected():
+    res = _spawn(_worker_bad_shard, 2)
+    for rank, ok, _, err in res:
+        assert err is None, err
+        assert ok, rank

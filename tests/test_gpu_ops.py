@@ -318,3 +318,39 @@ def test_fused_decode_layer_vs_oracle(w4, T, E, asym):
                       O.pack_zeros(c["z2"]) if asym else None, c["topk_ids"], c["topk_weights"])
     assert y.dtype == torch.float16
     assert max_abs_rel(y.float().cpu().numpy(), ref) <= MAX_ABS_REL
+
+
+def test_expert_parallel_layer_world1_vs_oracle(w4):
+    """ExpertParallelMoE on a one-rank NCCL group (dispatch -> local experts -> combine, plus a
+    replicated shared expert) against the oracle layer with the shared expert as expert E."""
+    import socket
+    from datetime import timedelta
+
+    import torch.distributed as dist
+    from w4a8_fp8_wmma.ep import ExpertParallelMoE
+    T, E, H, Ii, k = 16, 32, 2048, 512, 4
+    c = I.moe_layer_case(900, T, E + 1, H, Ii, k, 128)
+    # routed slots only over experts 0..E-1; expert E is the shared one
+    rng = np.random.default_rng(901)
+    ids = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
+    w = rng.random((T, k), dtype=np.float32)
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1,
+                            timeout=timedelta(seconds=60), device_id=torch.device("cuda", 0))
+    try:
+        p13, p2 = O.pack_int4(c["c13"]), O.pack_int4(c["c2"])
+        z13, z2 = O.pack_zeros(c["z13"]), O.pack_zeros(c["z2"])
+        wts = (cu(p13[:E]), cu(c["s13"][:E]), cu(z13[:E]), cu(p2[:E]), cu(c["s2"][:E]), cu(z2[:E]))
+        shared = (cu(p13[E:]), cu(c["s13"][E:]), cu(z13[E:]), cu(p2[E:]), cu(c["s2"][E:]),
+                  cu(z2[E:]))
+        layer = ExpertParallelMoE(*wts, E, k, shared=shared)
+        y = layer(cu(c["x"]), cu(ids), cu(w)).cpu().numpy()
+    finally:
+        dist.destroy_process_group()
+    ids_full = np.concatenate([ids, np.full((T, 1), E, np.int32)], axis=1)
+    w_full = np.concatenate([w, np.ones((T, 1), np.float32)], axis=1)
+    ref = O.moe_layer(c["x"], p13, c["s13"], z13, p2, c["s2"], z2, ids_full, w_full)
+    assert max_abs_rel(y, ref) <= MAX_ABS_REL
