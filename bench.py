@@ -201,7 +201,7 @@ def run_ours(args):
             step_fn()
         graph = g
     except Exception as exc:  # noqa: BLE001
-        print(f"[bench] graph capture failed ({type(exc).__name__}); timing eager steps",
+        print(f"[bench] graph capture failed ({type(exc).__name__}: {exc}); timing eager steps",
               file=sys.stderr)
         torch.cuda.synchronize()
     run = graph.replay if graph is not None else step_fn
@@ -239,8 +239,7 @@ def run_ours(args):
     e2e = end_to_end(torch, dist, args, world, dev, x_np, ids_np, w_np, layer, run_grouped_moe,
                      (w13, s13, z13, w2, s2, z2), E_total)
     if rank != 0:
-        dist.destroy_process_group()
-        return
+        _leave(dist, world)
     res = {
         "metric": "MoE-layer tokens/s (Qwen3.6-35B-A3B-shaped, decode T=32)"
         if args.workload == "decode" else "MoE-layer tokens/s (Qwen3.6-35B-A3B-shaped, prefill T=4096)",
@@ -266,9 +265,18 @@ def run_ours(args):
     }
     if world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(args.workload, budget_s=args.cpu_seconds)
-    print(json.dumps(res))
+    print(json.dumps(res), flush=True)
     if world > 1:
-        dist.destroy_process_group()
+        _leave(dist, world)
+
+
+def _leave(dist, world):
+    """End an EP rank: a last barrier, then exit without the NCCL teardown (which has been
+    seen to block after a failed graph capture)."""
+    dist.barrier()
+    sys.stdout.flush()
+    sys.stderr.flush()
+    os._exit(0)
 
 
 def _max_over_ranks(torch, dist, world, dev, v):

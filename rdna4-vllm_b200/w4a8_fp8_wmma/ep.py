@@ -36,7 +36,8 @@ def plan_dispatch(topk_ids: torch.Tensor, experts_per_rank: int, world: int, cap
     dest*capacity + pos. Pure tensor ops (no host sync)."""
     ids = topk_ids.reshape(-1).to(torch.int64)
     dest = torch.div(ids, experts_per_rank, rounding_mode="floor").clamp_(0, world - 1)
-    onehot = torch.nn.functional.one_hot(dest, world)          # (S, W)
+    # one-hot by comparison (F.one_hot validates its input with a device sync)
+    onehot = (dest[:, None] == torch.arange(world, device=ids.device)[None, :]).to(torch.int64)
     pos = (onehot.cumsum(0) - onehot).gather(1, dest[:, None]).squeeze(1)
     return dest, pos, dest * capacity + pos
 
@@ -59,6 +60,7 @@ class ExpertParallelMoE:
         self.w = (w13, s13, z13, w2, s2, z2)
         self.shared = shared  # (w13, s13, z13, w2, s2, z2) of one replicated shared expert
         self.expert_fn = expert_fn or self._gpu_experts
+        self._ntp = {}  # cached device scalars (no host->device copies inside graph capture)
 
     # ---- compute on received rows ------------------------------------------------------
     def _gpu_experts(self, rows: torch.Tensor, local_ids: torch.Tensor) -> torch.Tensor:
@@ -105,7 +107,10 @@ class ExpertParallelMoE:
         sorted_ids[row] = slots.to(torch.int32)
         tw = topk_weights.reshape(-1).to(torch.float32).contiguous()
         if back.is_cuda:
-            ntp = torch.tensor([W * C], dtype=torch.int32, device=dev)
+            key = (W * C, dev)
+            if key not in self._ntp:
+                self._ntp[key] = torch.full((1,), W * C, dtype=torch.int32, device=dev)
+            ntp = self._ntp[key]
             out = torch.ops.w4a8_fp8_wmma.mmq_fp8_moe_gather_reduce(back, sorted_ids, tw, ntp, k)
         else:  # CPU ranks (tests): same slot-order weighted sum
             out = torch.zeros((T, H), dtype=torch.float32)
