@@ -142,6 +142,32 @@ extern "C" int w4a8_mmq_fp8_gemm(const void* x, const int32_t* w_packed, const v
         sa.mode = kStreamStore;
         return launch_w4_stream(sa, st);
     }
+    if (kernel != W4A8_DENSE_REFERENCE_SCALAR && kernel != W4A8_DENSE_DECODE_GEMV && M > 32 &&
+        tc_path_ok(K, (int)group_size, weight_is_e2m1, w_packed, 1 << 20)) {
+        if (int rc = launch_operand_quant(x, OperandOut{s.xq, s.scales, nullptr, s.xsum}, M, K,
+                                          nullptr, st))
+            return rc;
+        cudaError_t ce = cudaMemsetAsync(s.counter, 0, sizeof(int), st);
+        if (ce != cudaSuccess) return (int)ce;
+        TcArgs t{};
+        t.xq = s.xq;
+        t.act_scales = s.scales;
+        t.xsum = s.xsum;
+        t.w = w_packed;
+        t.scales = static_cast<const __half*>(scales);
+        t.zeros = w_zeros;
+        t.out16 = static_cast<__half*>(out);
+        t.err = s.counter;
+        t.K = K;
+        t.N = (int)N;
+        t.G = G;
+        t.E = 1;
+        t.P = (int)M;
+        t.num_valid = (int)M;
+        t.top_k = 1;
+        t.block_m = 1 << 20;
+        return launch_w4_tc(t, st);
+    }
     if (int rc = launch_act_quant(x, s.xq, s.scales, M, K, st)) return rc;
     GemmArgs a{};
     a.x_fp8 = s.xq;
@@ -248,6 +274,37 @@ int moe_launch(const char* op, int epi, const void* x, const int32_t* w_packed,
             sa.mode = epi == kEpiSilu ? kStreamSilu : kStreamStore;
         }
         return launch_w4_stream(sa, st);
+    }
+    if (kernel == W4A8_MOE_WMMA && epi != kEpiScatter &&
+        tc_path_ok(K, (int)group_size, e2m1, w_packed, (int)block_m) &&
+        (epi != kEpiSilu || (N / 2) % 64 == 0)) {
+        if (int rc = launch_operand_quant(x, OperandOut{s.xq, s.scales, nullptr, s.xsum}, x_rows,
+                                          K, nullptr, st))
+            return rc;
+        cudaError_t ce = cudaMemsetAsync(s.counter, 0, sizeof(int), st);
+        if (ce != cudaSuccess) return (int)ce;
+        TcArgs t{};
+        t.xq = s.xq;
+        t.act_scales = s.scales;
+        t.xsum = s.xsum;
+        t.w = w_packed;
+        t.scales = static_cast<const __half*>(scales);
+        t.zeros = w_zeros;
+        t.sorted_ids = sorted_ids;
+        t.expert_ids = expert_ids;
+        t.ntp = ntp;
+        t.out16 = static_cast<__half*>(out);
+        t.err = s.counter;
+        t.K = K;
+        t.N = (int)N;
+        t.G = G;
+        t.E = (int)E;
+        t.P = (int)P;
+        t.num_valid = (int)(x_rows * top_k);
+        t.top_k = (int)top_k;
+        t.block_m = (int)block_m;
+        t.silu = epi == kEpiSilu ? 1 : 0;
+        return launch_w4_tc(t, st);
     }
     if (x_rows > 0)
         if (int rc = launch_act_quant(x, s.xq, s.scales, x_rows, K, st, row_limit)) return rc;

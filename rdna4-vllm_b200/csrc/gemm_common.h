@@ -86,6 +86,26 @@ struct StreamArgs {
 bool stream_path_ok(int64_t K, int G, int e2m1, const void* w);
 size_t stream_partials_bytes(int64_t P, int64_t N, int64_t K);
 int launch_w4_stream(StreamArgs a, cudaStream_t stream);
+
+// ---- tcgen05 tile GEMM (gemm_tc.cu) ----
+// Rows as in GemmArgs; activations are the operand quantiser's e4m3 bytes plus group sums.
+struct TcArgs {
+    const uint8_t* xq;          // (rows, K) e4m3
+    const float* act_scales;    // (rows,)
+    const float2* xsum;         // (rows, K/128) {K0, S}; S = sum of the group's activations
+    const int32_t* w;
+    const __half* scales;
+    const int32_t* zeros;
+    const int32_t* sorted_ids;
+    const int32_t* expert_ids;
+    const int32_t* ntp;
+    __half* out16;
+    int* err;                   // set to a non-zero code when a bounded wait gives up
+    int64_t K;
+    int N, G, E, P, num_valid, top_k, block_m, src_identity, silu;
+};
+bool tc_path_ok(int64_t K, int group_size, int e2m1, const void* w, int block_m);
+int launch_w4_tc(TcArgs a, cudaStream_t stream);
 // Quantise rows [0, min(M, row_limit)) of x (fp16) into the streaming GEMV operand format.
 int launch_operand_quant(const void* x, OperandOut o, int64_t M, int64_t K,
                          const int32_t* row_limit, cudaStream_t stream);

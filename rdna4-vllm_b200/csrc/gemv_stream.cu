@@ -388,7 +388,7 @@ __device__ void quant_operand_row(const __half* src, int64_t K, int64_t row, con
             out.y = *reinterpret_cast<const uint32_t*>(&d15);
             out.z = h26;
             out.w = *reinterpret_cast<const uint32_t*>(&d37);
-            reinterpret_cast<uint4*>(o.xh + row * K)[i] = out;
+            if (o.xh) reinterpret_cast<uint4*>(o.xh + row * K)[i] = out;
             const float2 f04 = __half22float2(*reinterpret_cast<const __half2*>(&h04));
             const float2 f26 = __half22float2(*reinterpret_cast<const __half2*>(&h26));
             const float2 f15 = __half22float2(*reinterpret_cast<const __half2*>(&h15));

@@ -23,7 +23,8 @@ from . import (moe_align_block_size, mmq_fp8_moe_gather_reduce, mmq_fp8_moe_gemm
 AWQ_REVERSE_PACK_ORDER = [0, 4, 1, 5, 2, 6, 3, 7]
 GEMV_MAX_M = int(os.environ.get("VLLM_ROCM_W4A8_FP8_WMMA_MOE_GEMV_MAX_M", "96"))
 GEMV_BLOCK_M = int(os.environ.get("VLLM_ROCM_W4A8_FP8_WMMA_MOE_GEMV_BLOCK_M", "8"))
-TILE_BLOCK_M = int(os.environ.get("VLLM_ROCM_W4A8_FP8_WMMA_MOE_BLOCK_M", "64"))
+# 128-row blocks feed the tcgen05 tile path N=128 MMAs (the reference uses 64 on gfx1201)
+TILE_BLOCK_M = int(os.environ.get("VLLM_ROCM_W4A8_FP8_WMMA_MOE_BLOCK_M", "128"))
 APPLY_CHUNK = int(os.environ.get("VLLM_ROCM_W4A8_FP8_WMMA_MOE_APPLY_CHUNK", "4096"))
 
 _MOE_IDS = {"scalar": 0, "wmma": 6, "gemv": 7}
