@@ -20,8 +20,9 @@ namespace {
 
 // Scratch layout of every GEMM entry point, in order (each 256-byte aligned):
 //   x_fp8 (rows, K) e4m3 | act_scales (rows,) f32 | xh (rows, K) fp16 | xsum (rows, K/128+1)
-//   float2 | counter | partials
-// xh, xsum and partials are used by the streaming GEMV path only.
+//   float2 | counter | partials | tile scratch
+// xh and partials are used by the streaming GEMV path only; the tile scratch (sorted-order
+// operand rows, see tc_carve) by the tcgen05 tile path only.
 struct Scratch {
     uint8_t* xq;
     float* scales;
@@ -29,13 +30,14 @@ struct Scratch {
     float2* xsum;
     int* counter;
     float* part;
+    void* tc;
 };
 
 size_t scratch_bytes(int64_t rows, int64_t K, int64_t P, int64_t N) {
     return align_up((size_t)rows * (size_t)K, 256) + align_up((size_t)rows * 4, 256) +
            align_up((size_t)rows * (size_t)K * 2, 256) +
            align_up((size_t)rows * (size_t)(K / 128 + 1) * 8, 256) + 256 +
-           stream_partials_bytes(P, N, K);
+           stream_partials_bytes(P, N, K) + tc_scratch_bytes(P, K);
 }
 
 bool carve(void* ws, size_t ws_bytes, int64_t rows, int64_t K, int64_t P, int64_t N,
@@ -53,6 +55,8 @@ bool carve(void* ws, size_t ws_bytes, int64_t rows, int64_t K, int64_t P, int64_
     s.counter = reinterpret_cast<int*>(p);
     p += 256;
     s.part = reinterpret_cast<float*>(p);
+    p += stream_partials_bytes(P, N, K);
+    s.tc = p;
     return true;
 }
 
@@ -166,6 +170,7 @@ extern "C" int w4a8_mmq_fp8_gemm(const void* x, const int32_t* w_packed, const v
         t.num_valid = (int)M;
         t.top_k = 1;
         t.block_m = 1 << 20;
+        tc_carve(s.tc, M, K, t);
         return launch_w4_tc(t, st);
     }
     if (int rc = launch_act_quant(x, s.xq, s.scales, M, K, st)) return rc;
@@ -304,6 +309,7 @@ int moe_launch(const char* op, int epi, const void* x, const int32_t* w_packed,
         t.top_k = (int)top_k;
         t.block_m = (int)block_m;
         t.silu = epi == kEpiSilu ? 1 : 0;
+        tc_carve(s.tc, P, K, t);
         return launch_w4_tc(t, st);
     }
     if (x_rows > 0)

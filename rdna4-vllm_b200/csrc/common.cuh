@@ -92,12 +92,14 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
 // vLLM silu_and_mul on fp16 tensors: gate/up are the fp16 stores of the GEMM, silu is
 // evaluated in fp32 and rounded to fp16, the product is a half*half multiply (the reference's
 // moe_silu_and_mul_h, w4a8_fp8_wmma/moe_kernel.hip:555-565; oracle test_moe_experts.py:274-280).
-__device__ __forceinline__ __half silu_and_mul_half(float gate_f, float up_f) {
-    const __half gh = __float2half_rn(gate_f);
-    const __half uh = __float2half_rn(up_f);
+// The same on operands already rounded to fp16.
+__device__ __forceinline__ __half silu_mul_h(__half gh, __half uh) {
     const float g = __half2float(gh);
     const __half sh = __float2half_rn(__fdiv_rn(g, 1.0f + expf(-g)));
     return __hmul(sh, uh);
+}
+__device__ __forceinline__ __half silu_and_mul_half(float gate_f, float up_f) {
+    return silu_mul_h(__float2half_rn(gate_f), __float2half_rn(up_f));
 }
 
 // OCP E2M1 (mxfp4) code -> value; the table is the format definition (bit3 sign,

@@ -90,9 +90,12 @@ int launch_w4_stream(StreamArgs a, cudaStream_t stream);
 // ---- tcgen05 tile GEMM (gemm_tc.cu) ----
 // Rows as in GemmArgs; activations are the operand quantiser's e4m3 bytes plus group sums.
 struct TcArgs {
-    const uint8_t* xq;          // (rows, K) e4m3
+    const uint8_t* xq;          // (rows, K) e4m3, one row per source token
     const float* act_scales;    // (rows,)
     const float2* xsum;         // (rows, K/128) {K0, S}; S = sum of the group's activations
+    uint8_t* xs;                // scratch (P_pad, K): sorted-order e4m3 rows (tc_carve)
+    float* asc_s;               // scratch (P_pad,): sorted-order activation scales
+    float* ssum;                // scratch (K/128, P_pad): sorted-order group sums, group-major
     const int32_t* w;
     const __half* scales;
     const int32_t* zeros;
@@ -102,9 +105,12 @@ struct TcArgs {
     __half* out16;
     int* err;                   // set to a non-zero code when a bounded wait gives up
     int64_t K;
-    int N, G, E, P, num_valid, top_k, block_m, src_identity, silu;
+    int N, G, E, P, P_pad, num_valid, top_k, block_m, src_identity, silu;
 };
 bool tc_path_ok(int64_t K, int group_size, int e2m1, const void* w, int block_m);
+// Scratch of the tile path for P sorted rows: carved by tc_carve into xs / asc_s / ssum.
+size_t tc_scratch_bytes(int64_t P, int64_t K);
+void tc_carve(void* base, int64_t P, int64_t K, TcArgs& t);
 int launch_w4_tc(TcArgs a, cudaStream_t stream);
 // Quantise rows [0, min(M, row_limit)) of x (fp16) into the streaming GEMV operand format.
 int launch_operand_quant(const void* x, OperandOut o, int64_t M, int64_t K,

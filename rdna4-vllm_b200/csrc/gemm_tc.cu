@@ -1,28 +1,39 @@
 // gemm_tc.cu — W4A8 (grouped) GEMM tile path on the 5th-generation tensor cores (tcgen05).
 //
-// Tile = 128 weight rows x NT activation rows (NT = 64 or 128, never straddling an expert
-// block of the padded-sorted layout). The MMA runs "swap-AB": A = the 128 dequantised weight
-// rows (TMEM lanes), B = the NT gathered e4m3 activation rows (TMEM columns), both K-major in
-// the no-swizzle core-matrix layout, one tcgen05.mma.cta_group::1.kind::f8f6f4 per 32-wide K
-// slice, fp32 accumulators in tensor memory.
+// Two launches:
+//   1. tc_gather_kernel — copies each sorted row's e4m3 activation row, its activation scale and
+//      its per-group sums S into dense sorted-order buffers (padding rows become zeros), so the
+//      GEMM reads its token tiles with plain 2D TMA boxes instead of per-row gathers.
+//   2. w4_tc_kernel — persistent and warp-specialised, one CTA per SM. A tile is 128 weight
+//      rows x NT sorted rows (NT = 64 or 128; a tile never straddles an expert block). Tiles are
+//      dealt round-robin to the CTAs; inside a CTA every role walks the same tile sequence and
+//      the (tile, K-group) steps flow through mbarrier rings, so the next tile's loads and MMAs
+//      overlap the current tile's epilogue.
 //
-// Numerics. The weight operand holds e4m3(q) — the unsigned 4-bit code itself, exact in e4m3 —
-// so per 128-wide group g the tensor core returns acc = sum_k q_k a_k. With S_g = sum_k a_k
-// (from the operand quantiser) the reference's group result sum_k (q_k - z) a_k equals
-// acc - z*S_g exactly in real arithmetic, and it is folded in fp32 as
+// Roles (16 warps):
+//   warp 0      TMA producer: weight codes (2D box, 64-byte swizzle), token tile (2D box,
+//               128-byte swizzle = the UMMA K-major SW128 layout), group sums (bulk copy).
+//   warp 1      MMA issuer: 4 x tcgen05.mma.kind::f8f6f4 (K = 32 each) per group into one of the
+//               TMEM accumulators (512 columns / NT), committed to the stage / A / accumulator barriers.
+//   warp 2      owns the tensor-memory allocation.
+//   warps 4-7   expand the 4-bit codes to e4m3 bytes in the SW128 A layout (thread = weight row).
+//   warps 8-15  fold each group's accumulator into fp32 registers and write the tile's output.
+//
+// Numerics. The A operand holds e4m3(q) — the unsigned 4-bit code itself, exact in e4m3 — so
+// per 128-wide group g the tensor core returns acc = sum_k q_k a_k. With S_g = sum_k a_k the
+// reference's group result sum_k (q_k - z) a_k equals acc - z*S_g exactly in real arithmetic,
+// and it is folded in fp32 as
 //     tot += scale[n,g] * acc - (scale[n,g] * z) * S_g
 // then multiplied by the row's activation scale: the reference oracle's association
 // (w4a8_fp8_wmma/test_correctness.py:113-119) up to fp32 rounding.
 //
-// Pipeline per K group g (all 256 threads, one CTA per tile):
-//   1. cp.async ring (3 stages) already holds group g's packed codes, token tile and sums;
-//   2. threads expand the codes to e4m3 bytes in shared memory (3 prmt + 1 lop3 per 4 codes);
-//   3. one thread issues the 4 MMAs of group g into TMEM buffer g%2 and commits them to an
-//      mbarrier; meanwhile every thread folds group g-1 from the other TMEM buffer
-//      (tcgen05.ld) and issues the cp.async of group g+2.
-// Every mbarrier wait is bounded; on timeout the kernel records an error code and finishes
-// without further waits, always releasing its tensor memory.
+// Every mbarrier wait is bounded. When one gives up the kernel records an error code, every
+// role stops waiting (the results are then garbage, reported through TcArgs::err), the producer
+// waits boundedly for its own copies in flight and the tensor memory is always released.
+#include <cudaTypedefs.h>
+
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "gemm_common.h"
@@ -32,46 +43,56 @@ namespace w4a8 {
 
 namespace {
 
-constexpr int kTcThreads = 256;
-constexpr int kStages = 3;          // cp.async ring depth
-constexpr int kRawStride = 64;      // bytes per weight row in the raw-code ring
+constexpr int kTcThreads = 512;
+constexpr uint32_t kSpinLimit = 1u << 22;
+constexpr int kFoldWarps = 8;
 
-// 16-byte chunk j of raw row m is stored at chunk j ^ ((m >> 1) & 3): the expansion step reads
-// 8 consecutive rows per quarter-warp without bank conflicts.
-__device__ __forceinline__ int raw_off(int m, int j) { return m * 64 + ((j ^ ((m >> 1) & 3)) << 4); }
-constexpr uint32_t kSpinLimit = 1u << 24;
+template <int NT>
+struct TcCfg {
+    static constexpr int kStages = NT == 128 ? 5 : 7;  // TMA ring depth (codes + tokens)
+    static constexpr int kAStages = NT == 128 ? 4 : 5; // dequantised-A ring depth
+    static constexpr int kSStages = 8;                 // group-sum ring depth
+    static constexpr int kAcc = 512 / NT;              // TMEM accumulators (all 512 columns)
+    static constexpr int kCols = NT / 2;               // accumulator columns per fold thread
+    static constexpr uint32_t kTmemCols = 512;
+    static constexpr uint32_t kStageBytes = 128 * 64 + NT * 128;
+};
 
 template <int NT>
 struct TcSmem {
-    uint8_t a[2][128 * 128];                 // e4m3 weights, core-matrix layout
-    uint8_t b[kStages][NT * 128];            // e4m3 activations, core-matrix layout
-    uint8_t raw[kStages][128 * kRawStride];  // packed int4 codes of the tile's 128 rows
-    float ssum[kStages + 1][NT];             // per-group activation sums S
-    float asc[NT];
-    int src[NT];
-    uint64_t mbar[2];
+    uint8_t b[TcCfg<NT>::kStages][NT * 128];     // token tiles, SW128 K-major (1024-aligned)
+    uint8_t a[TcCfg<NT>::kAStages][128 * 128];   // e4m3 weights, SW128 K-major
+    uint8_t raw[TcCfg<NT>::kStages][128 * 64];   // packed codes, SW64 as TMA writes them
+    __half otile[NT * 128];                      // epilogue: fp16 results, [column][row]
+    float ssum[TcCfg<NT>::kSStages][NT];         // group sums S of the tile's rows
+    uint64_t full[TcCfg<NT>::kStages];
+    uint64_t empty[TcCfg<NT>::kStages];
+    uint64_t sfull[TcCfg<NT>::kSStages];
+    uint64_t sempty[TcCfg<NT>::kSStages];
+    uint64_t afull[TcCfg<NT>::kAStages];
+    uint64_t aempty[TcCfg<NT>::kAStages];
+    uint64_t tfull[TcCfg<NT>::kAcc];
+    uint64_t tempty[TcCfg<NT>::kAcc];
     uint32_t tmem_base;
-    int any;
-    int bad;                                 // a bounded wait gave up
+    int bad;
 };
 
-// Byte offset of (row r, 16-byte K chunk j) in a 128-byte-wide K-major core-matrix tile:
-// core matrices are 8 rows x 16 bytes contiguous; K-adjacent ones are 128 B apart (LBO),
-// 8-row groups are 1024 B apart (SBO).
-__device__ __forceinline__ int cm_off(int r, int j) {
-    return ((r >> 3) * 8 + j) * 128 + (r & 7) * 16;
-}
+static_assert(sizeof(TcSmem<128>) + 1024 <= 227 * 1024, "tile kernel shared memory");
+static_assert(sizeof(TcSmem<64>) + 1024 <= 227 * 1024, "tile kernel shared memory");
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
 }
 
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
+// UMMA shared-memory descriptor, K-major with the 128-byte swizzle: 8-row atoms of 128 bytes,
+// atoms 1024 bytes apart (SBO); the leading offset is unused for swizzled K-major operands.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
     uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
-    d |= (uint64_t)((128u >> 4) & 0x3FFFu) << 16;   // leading byte offset (K direction)
-    d |= (uint64_t)((1024u >> 4) & 0x3FFFu) << 32;  // stride byte offset (8-row groups)
-    d |= (uint64_t)1 << 46;                         // descriptor version for sm_100
-    return d;                                       // base offset 0, SWIZZLE_NONE
+    d |= (uint64_t)1 << 16;
+    d |= (uint64_t)((1024u >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;  // descriptor version (sm_100)
+    d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+    return d;
 }
 
 // kind::f8f6f4 instruction descriptor: fp32 accumulate, A = B = e4m3, both K-major.
@@ -79,29 +100,56 @@ __host__ __device__ constexpr uint32_t umma_idesc(int M, int N) {
     return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)),
-                 "l"(gmem), "r"(pred ? 16 : 0));
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }
-__device__ __forceinline__ void cp_async4(void* smem, const void* gmem, bool pred) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(smem)),
-                 "l"(gmem), "r"(pred ? 4 : 0));
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+// Bounded wait; once any wait in the CTA has given up, later waits return at once.
+__device__ __forceinline__ void mbar_wait(uint64_t* bar, uint32_t parity, volatile int* bad) {
+    if (*bad) return;
+    for (uint32_t i = 0; i < kSpinLimit; ++i)
+        if (mbar_try(bar, parity)) return;
+    *bad = 1;
 }
 
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    const uint32_t addr = smem_u32(bar);
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
-        uint32_t done;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(done)
-            : "r"(addr), "r"(parity)
-            : "memory");
-        if (done) return true;
-    }
-    return false;
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
 }
 
 // 4 codes (the low 16 bits of `w`, nibble i = code i) -> 4 e4m3 bytes of the codes' values.
@@ -118,272 +166,433 @@ __device__ __forceinline__ uint32_t codes_to_e4m3(uint32_t w) {
     return lop3<(0xF0 & 0xCC) | (~0xF0 & 0xAA)>(m, hi, lo); // m ? hi : lo, bitwise
 }
 
-template <int NT>
-__device__ __forceinline__ void issue_stage(const TcArgs& a, TcSmem<NT>& sm, int e, int mt, int g,
-                                            int st, int ss, int r0) {
-    const int tid = threadIdx.x;
-    if (g < a.G) {
-        // token tile: NT rows x 8 chunks of 16 bytes
-        for (int i = tid; i < NT * 8; i += kTcThreads) {
-            const int r = i >> 3, j = i & 7;
-            const int src = sm.src[r];
-            const uint8_t* gp = a.xq + (int64_t)max(src, 0) * a.K + (int64_t)g * 128 + j * 16;
-            cp_async16(&sm.b[st][cm_off(r, j)], gp, src >= 0);
-        }
-        // packed codes: 128 rows x 4 chunks of 16 bytes
-        const int64_t kw = a.K / 8;
-        for (int i = tid; i < 128 * 4; i += kTcThreads) {
-            const int m = i >> 2, j = i & 3;
-            int n;
-            if (a.silu) n = (m < 64) ? mt * 64 + m : a.N / 2 + mt * 64 + (m - 64);
-            else n = mt * 128 + m;
-            const bool ok = n < a.N;
-            const int32_t* gp = a.w + ((int64_t)e * a.N + (ok ? n : 0)) * kw + g * 16 + j * 4;
-            cp_async16(&sm.raw[st][raw_off(m, j)], gp, ok);
-        }
-        // activation sums S of the group
-        for (int i = tid; i < NT; i += kTcThreads) {
-            const int src = sm.src[i];
-            const float* gp = reinterpret_cast<const float*>(a.xsum + (int64_t)max(src, 0) * a.G + g) + 1;
-            cp_async4(&sm.ssum[ss][i], gp, src >= 0);
-        }
-    }
-    asm volatile("cp.async.commit_group;" ::);
+// d = a * b + c on two fp32 lanes at once.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;"
+        : "=l"(d)
+        : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)),
+          "l"(*reinterpret_cast<uint64_t*>(&c)));
+    return *reinterpret_cast<float2*>(&d);
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,"
+        "%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31},"
+        " [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+          "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
+          "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]),
+          "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]),
+          "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Expert of tile row block rb (0 for the dense GEMM).
+__device__ __forceinline__ int tile_expert(const TcArgs& a, int rb, int NT) {
+    if (!a.expert_ids) return 0;
+    return a.expert_ids[(int64_t)rb * NT / a.block_m];
 }
 
 template <int NT>
-__global__ void __launch_bounds__(kTcThreads, 2) w4_tc_kernel(const TcArgs a) {
-    extern __shared__ __align__(1024) uint8_t smem_raw[];
-    TcSmem<NT>& sm = *reinterpret_cast<TcSmem<NT>*>(smem_raw);
+__global__ void __launch_bounds__(kTcThreads, 1)
+w4_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmw,
+             const __grid_constant__ CUtensorMap tmx) {
+    using C = TcCfg<NT>;
+    extern __shared__ uint8_t smem_raw[];
+    TcSmem<NT>& sm = *reinterpret_cast<TcSmem<NT>*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int mt = blockIdx.x;
-    const int r0 = blockIdx.y * NT;
-    const int n_out = a.silu ? a.N / 2 : a.N;
-    const int P_valid = a.ntp ? min(a.ntp[0], a.P) : a.P;
-    if (r0 >= P_valid) return;  // rows past num_tokens_post_padded are unspecified
-    const int e = a.expert_ids ? a.expert_ids[r0 / a.block_m] : 0;
-    if (tid == 0) {
-        sm.any = 0;
-        sm.bad = 0;
-    }
-    __syncthreads();
-    for (int i = tid; i < NT; i += kTcThreads) {
-        const int r = r0 + i;
-        int src = -1;
-        float asc = 0.f;
-        if (r < P_valid && e >= 0 && e < a.E) {
-            const int sid = a.sorted_ids ? a.sorted_ids[r] : r;
-            if (sid >= 0 && sid < a.num_valid) {
-                src = a.src_identity ? r : sid / a.top_k;
-                asc = a.act_scales[src];
-                sm.any = 1;
-            }
-        }
-        sm.src[i] = src;
-        sm.asc[i] = asc;
-    }
-    __syncthreads();
-    // output rows handled by this thread in the epilogue
-    const int lg = warp & 3;        // TMEM lane group: lanes 32*lg .. 32*lg+31
-    const int half = warp >> 2;     // column half
-    const int m = lg * 32 + lane;   // tile row = TMEM lane
-    int n;                          // weight row of m
-    bool up_row = false;
-    if (a.silu) {
-        up_row = m >= 64;
-        n = up_row ? a.N / 2 + mt * 64 + (m - 64) : mt * 64 + m;
-    } else {
-        n = mt * 128 + m;
-    }
-    const int n_store = a.silu ? mt * 64 + (m & 63) : n;
-    constexpr int kCols = NT / 2;
-    const int c0 = half * kCols;
-    if (!sm.any) {  // all-padding tile or non-local expert: zeros
-        if (!(a.silu && up_row) && n_store < n_out)
-#pragma unroll 1
-            for (int c = 0; c < kCols; ++c)
-                if (r0 + c0 + c < P_valid)
-                    a.out16[(int64_t)(r0 + c0 + c) * n_out + n_store] = __float2half_rn(0.f);
-        return;
-    }
+    volatile int* bad = &sm.bad;
 
-    // ---- tensor memory + barriers ----
-    constexpr uint32_t kTmemCols = 2 * NT;
-    if (warp == 0) {
+    const int P_valid = a.ntp ? min(a.ntp[0], a.P) : a.P;
+    const int nblk = (P_valid + NT - 1) / NT;
+    const int n_mt = a.silu ? (a.N / 2) / 64 : (a.N + 127) / 128;
+    const int n_tiles = nblk * n_mt;
+    const int n_out = a.silu ? a.N / 2 : a.N;
+
+    if (tid == 0) {
+        sm.bad = 0;
+        for (int s = 0; s < C::kStages; ++s) {
+            mbar_init(&sm.full[s], 1);
+            mbar_init(&sm.empty[s], 1);
+        }
+        for (int s = 0; s < C::kSStages; ++s) {
+            mbar_init(&sm.sfull[s], 1);
+            mbar_init(&sm.sempty[s], kFoldWarps);
+        }
+        for (int s = 0; s < C::kAStages; ++s) {
+            mbar_init(&sm.afull[s], 4);
+            mbar_init(&sm.aempty[s], 1);
+        }
+        for (int s = 0; s < C::kAcc; ++s) {
+            mbar_init(&sm.tfull[s], 1);
+            mbar_init(&sm.tempty[s], kFoldWarps);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 2) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(&sm.tmem_base)),
-                     "r"(kTmemCols));
+                     "r"(C::kTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
-    }
-    if (tid == 0) {
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&sm.mbar[0])));
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&sm.mbar[1])));
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::);
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::);
     const uint32_t tmem = sm.tmem_base;
 
-    const bool row_ok = n < a.N;
-    const int64_t sc_base = ((int64_t)e * a.N + (row_ok ? n : 0)) * a.G;
-    const int32_t* zrow = a.zeros ? a.zeros + ((int64_t)e * (a.N / 8) + ((row_ok ? n : 0) >> 3)) * a.G
-                                  : nullptr;
-    const int zsh = ((row_ok ? n : 0) & 7) * 4;
-    float tot[kCols];
-#pragma unroll
-    for (int c = 0; c < kCols; ++c) tot[c] = 0.f;
-
-    for (int s = 0; s < kStages - 1; ++s) issue_stage<NT>(a, sm, e, mt, s, s, s, r0);
-    // scale/zero of group g-1 (folded in iteration g) and of group g (loaded one ahead)
-    float s_fold = 0.f, z_fold = 8.f;
-    float s_next = __half2float(a.scales[sc_base]);
-    float z_next = zrow ? (float)((__ldg(zrow) >> zsh) & 0xF) : 8.f;
-    const uint32_t idesc = umma_idesc(128, NT);
-    bool bad = false;
-
-    auto fold = [&](int gf, float sv, float zv) {
-        // wait for the MMAs of group gf, then fold its TMEM buffer
-        if (!bad && !mbar_wait(&sm.mbar[gf & 1], (uint32_t)((gf >> 1) & 1))) {
-            bad = true;
-            atomicOr(&sm.bad, 1);
-        }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::);
-        const float sz = sv * zv;
-        const float* S = sm.ssum[gf % (kStages + 1)] + c0;
-#pragma unroll
-        for (int cc = 0; cc < kCols; cc += 32) {
-            uint32_t v[32];
-            const uint32_t taddr =
-                tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)((gf & 1) * NT + c0 + cc);
-            asm volatile(
-                "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,"
-                "%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31},"
-                " [%32];"
-                : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
-                  "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]),
-                  "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]),
-                  "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
-                  "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]),
-                  "=r"(v[30]), "=r"(v[31])
-                : "r"(taddr));
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-                const float4 s4 = *reinterpret_cast<const float4*>(S + cc + j);
-                tot[cc + j + 0] = fmaf(sv, __uint_as_float(v[j + 0]), fmaf(-sz, s4.x, tot[cc + j + 0]));
-                tot[cc + j + 1] = fmaf(sv, __uint_as_float(v[j + 1]), fmaf(-sz, s4.y, tot[cc + j + 1]));
-                tot[cc + j + 2] = fmaf(sv, __uint_as_float(v[j + 2]), fmaf(-sz, s4.z, tot[cc + j + 2]));
-                tot[cc + j + 3] = fmaf(sv, __uint_as_float(v[j + 3]), fmaf(-sz, s4.w, tot[cc + j + 3]));
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            uint32_t it = 0;
+            for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+                const int rb = t / n_mt, mt = t % n_mt;
+                const int e = tile_expert(a, rb, NT);
+                if (e < 0 || e >= a.E) continue;
+                const int r0 = rb * NT;
+                // warm L2 with this CTA's next tile (weights and tokens) while this one runs
+                const int tn = t + gridDim.x;
+                if (tn < n_tiles) {
+                    const int rbn = tn / n_mt, mtn = tn % n_mt;
+                    const int en = tile_expert(a, rbn, NT);
+                    if (en >= 0 && en < a.E)
+                        for (int g = 0; g < a.G; ++g) {
+                            if (a.silu) {
+                                tma_prefetch_2d(&tmw, g * 64, en * a.N + mtn * 64);
+                                tma_prefetch_2d(&tmw, g * 64, en * a.N + a.N / 2 + mtn * 64);
+                            } else {
+                                tma_prefetch_2d(&tmw, g * 64, en * a.N + mtn * 128);
+                            }
+                            tma_prefetch_2d(&tmx, g * 128, rbn * NT);
+                        }
+                }
+                for (int g = 0; g < a.G; ++g, ++it) {
+                    const int s = it % C::kStages;
+                    const int ss = it % C::kSStages;
+                    mbar_wait(&sm.empty[s], ((it / C::kStages) & 1) ^ 1, bad);
+                    mbar_expect_tx(&sm.full[s], C::kStageBytes);
+                    if (a.silu) {
+                        tma_load_2d(&sm.raw[s][0], &tmw, g * 64, e * a.N + mt * 64, &sm.full[s]);
+                        tma_load_2d(&sm.raw[s][64 * 64], &tmw, g * 64,
+                                    e * a.N + a.N / 2 + mt * 64, &sm.full[s]);
+                    } else {
+                        tma_load_2d(&sm.raw[s][0], &tmw, g * 64, e * a.N + mt * 128, &sm.full[s]);
+                    }
+                    tma_load_2d(&sm.b[s][0], &tmx, g * 128, r0, &sm.full[s]);
+                    mbar_wait(&sm.sempty[ss], ((it / C::kSStages) & 1) ^ 1, bad);
+                    mbar_expect_tx(&sm.sfull[ss], NT * 4);
+                    bulk_load(&sm.ssum[ss][0], a.ssum + (int64_t)g * a.P_pad + r0, NT * 4,
+                              &sm.sfull[ss]);
+                }
+            }
+            // leave no copy in flight: wait (boundedly) for the last ring's worth of loads
+            if (*bad) {
+                const uint32_t first = it > (uint32_t)C::kStages ? it - C::kStages : 0;
+                for (uint32_t j = first; j < it; ++j)
+                    for (uint32_t i = 0; i < kSpinLimit; ++i)
+                        if (mbar_try(&sm.full[j % C::kStages], (j / C::kStages) & 1)) break;
+                const uint32_t sfirst = it > (uint32_t)C::kSStages ? it - C::kSStages : 0;
+                for (uint32_t j = sfirst; j < it; ++j)
+                    for (uint32_t i = 0; i < kSpinLimit; ++i)
+                        if (mbar_try(&sm.sfull[j % C::kSStages], (j / C::kSStages) & 1)) break;
             }
         }
-        asm volatile("tcgen05.fence::before_thread_sync;" ::);
-    };
-
-    for (int g = 0; g < a.G; ++g) {
-        const int st = g % kStages;
-        asm volatile("cp.async.wait_group %0;" ::"n"(kStages - 2));
-        __syncthreads();  // group g's codes, tokens and sums have landed for everyone
-        {
-            // expand codes -> e4m3 bytes: thread handles row mm, 32 codes (half hh of the group)
-            const int mm = tid & 127, hh = tid >> 7;
-            const uint4 rw0 = *reinterpret_cast<const uint4*>(&sm.raw[st][raw_off(mm, 2 * hh)]);
-            const uint4 rw1 = *reinterpret_cast<const uint4*>(&sm.raw[st][raw_off(mm, 2 * hh + 1)]);
-            const uint32_t wv[8] = {rw0.x, rw0.y, rw0.z, rw0.w, rw1.x, rw1.y, rw1.z, rw1.w};
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc(128, NT);
+            uint32_t it = 0;
+            for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+                const int e = tile_expert(a, t / n_mt, NT);
+                if (e < 0 || e >= a.E) continue;
+                for (int g = 0; g < a.G; ++g, ++it) {
+                    const int s = it % C::kStages;
+                    const int as = it % C::kAStages;
+                    const int tb = it % C::kAcc;
+                    mbar_wait(&sm.full[s], (it / C::kStages) & 1, bad);
+                    mbar_wait(&sm.afull[as], (it / C::kAStages) & 1, bad);
+                    mbar_wait(&sm.tempty[tb], ((it / C::kAcc) & 1) ^ 1, bad);
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::);
+                    const uint32_t a0 = smem_u32(&sm.a[as][0]);
+                    const uint32_t b0 = smem_u32(&sm.b[s][0]);
+                    const uint32_t d = tmem + (uint32_t)(tb * NT);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {  // 16 codes -> one 16-byte chunk
-                uint4 o;
-                o.x = codes_to_e4m3(wv[2 * q]);
-                o.y = codes_to_e4m3(wv[2 * q] >> 16);
-                o.z = codes_to_e4m3(wv[2 * q + 1]);
-                o.w = codes_to_e4m3(wv[2 * q + 1] >> 16);
-                *reinterpret_cast<uint4*>(&sm.a[g & 1][cm_off(mm, hh * 4 + q)]) = o;
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint64_t da = desc_sw128(a0 + kk * 32);
+                        const uint64_t db = desc_sw128(b0 + kk * 32);
+                        const uint32_t acc = kk > 0 ? 1u : 0u;
+                        asm volatile(
+                            "{\n\t.reg .pred p;\n\t"
+                            "setp.ne.b32 p, %4, 0;\n\t"
+                            "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+                            "l"(da), "l"(db), "r"(idesc), "r"(acc));
+                    }
+                    asm volatile(
+                        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                        ::"r"(smem_u32(&sm.empty[s])));
+                    asm volatile(
+                        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                        ::"r"(smem_u32(&sm.aempty[as])));
+                    asm volatile(
+                        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                        ::"r"(smem_u32(&sm.tfull[tb])));
+                }
             }
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncthreads();
-        if (tid == 0) {
-            asm volatile("tcgen05.fence::after_thread_sync;" ::);
-            const uint32_t a0 = smem_u32(&sm.a[g & 1][0]);
-            const uint32_t b0 = smem_u32(&sm.b[st][0]);
-            const uint32_t d = tmem + (uint32_t)((g & 1) * NT);
+    } else if (warp >= 4 && warp < 8) {
+        // ---------------- code expansion: thread = weight row ----------------
+        const int m = tid - 128;
+        const int sw64 = (m >> 1) & 3, sw128 = m & 7;
+        uint32_t it = 0;
+        for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+            const int e = tile_expert(a, t / n_mt, NT);
+            if (e < 0 || e >= a.E) continue;
+            for (int g = 0; g < a.G; ++g, ++it) {
+                const int s = it % C::kStages;
+                const int as = it % C::kAStages;
+                mbar_wait(&sm.full[s], (it / C::kStages) & 1, bad);
+                mbar_wait(&sm.aempty[as], ((it / C::kAStages) & 1) ^ 1, bad);
+                const uint8_t* rr = &sm.raw[s][m * 64];
+                uint8_t* ar = &sm.a[as][m * 128];
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                const uint64_t da = umma_desc(a0 + kk * 256);
-                const uint64_t db = umma_desc(b0 + kk * 256);
-                const uint32_t acc = kk > 0 ? 1u : 0u;
-                asm volatile(
-                    "{\n\t.reg .pred p;\n\t"
-                    "setp.ne.b32 p, %4, 0;\n\t"
-                    "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
-                    "l"(da), "l"(db), "r"(idesc), "r"(acc));
+                for (int j = 0; j < 4; ++j) {  // 32 codes -> two 16-byte e4m3 chunks
+                    const uint4 w = *reinterpret_cast<const uint4*>(rr + ((j ^ sw64) << 4));
+                    uint4 o0, o1;
+                    o0.x = codes_to_e4m3(w.x);
+                    o0.y = codes_to_e4m3(w.x >> 16);
+                    o0.z = codes_to_e4m3(w.y);
+                    o0.w = codes_to_e4m3(w.y >> 16);
+                    o1.x = codes_to_e4m3(w.z);
+                    o1.y = codes_to_e4m3(w.z >> 16);
+                    o1.z = codes_to_e4m3(w.w);
+                    o1.w = codes_to_e4m3(w.w >> 16);
+                    *reinterpret_cast<uint4*>(ar + (((2 * j) ^ sw128) << 4)) = o0;
+                    *reinterpret_cast<uint4*>(ar + (((2 * j + 1) ^ sw128) << 4)) = o1;
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm.afull[as]);
             }
-            asm volatile(
-                "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                    smem_u32(&sm.mbar[g & 1])));
         }
-        if (g > 0) fold(g - 1, s_fold, z_fold);  // overlaps the MMAs of group g
-        s_fold = s_next;
-        z_fold = z_next;
-        if (g + 1 < a.G) {
-            s_next = __half2float(a.scales[sc_base + g + 1]);
-            if (zrow) z_next = (float)((__ldg(zrow + g + 1) >> zsh) & 0xF);
-        }
-        issue_stage<NT>(a, sm, e, mt, g + kStages - 1, (g + kStages - 1) % kStages,
-                        (g + kStages - 1) % (kStages + 1), r0);
-    }
-    fold(a.G - 1, s_fold, z_fold);
-    asm volatile("cp.async.wait_all;" ::);
-    __syncthreads();
-
-    // ---- epilogue: out[row][n] = fp16(tot * a_scale) (or SiLU of the gate/up pair) ----
-    if (a.silu) {
-        __half* up = reinterpret_cast<__half*>(&sm.a[0][0]);  // 64 x NT halves
-        if (up_row)
+    } else if (warp >= 8) {
+        // ---------------- fold + epilogue ----------------
+        constexpr int kCols = C::kCols;
+        const int q = warp & 3;                     // TMEM lane quadrant
+        const int c0 = ((warp - 8) >> 2) * kCols;   // column half
+        const int m = q * 32 + lane;                // tile row = TMEM lane
+        const bool up_row = a.silu && m >= 64;
+        uint32_t it = 0;
+        for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+            const int rb = t / n_mt, mt = t % n_mt;
+            const int e = tile_expert(a, rb, NT);
+            const int r0 = rb * NT;
+            int n;
+            if (a.silu) n = up_row ? a.N / 2 + mt * 64 + (m - 64) : mt * 64 + m;
+            else n = mt * 128 + m;
+            const int n_store = a.silu ? mt * 64 + (m & 63) : n;
+            if (e < 0 || e >= a.E) {  // non-local expert: zeros
+                if (!up_row && n_store < n_out)
+#pragma unroll 4
+                    for (int c = 0; c < kCols; ++c)
+                        if (r0 + c0 + c < P_valid)
+                            a.out16[(int64_t)(r0 + c0 + c) * n_out + n_store] = __float2half_rn(0.f);
+                continue;
+            }
+            const int nn = n < a.N ? n : 0;
+            const __half* srow = a.scales + ((int64_t)e * a.N + nn) * a.G;
+            const int32_t* zrow =
+                a.zeros ? a.zeros + ((int64_t)e * (a.N / 8) + (nn >> 3)) * a.G : nullptr;
+            const int zsh = (nn & 7) * 4;
+            // activation scales of the tile's columns: lane l holds columns c0 + l (+ 32)
+            float asc_l[kCols / 32];
+#pragma unroll
+            for (int i = 0; i < kCols / 32; ++i) asc_l[i] = __ldg(a.asc_s + r0 + c0 + i * 32 + lane);
+            float tot[kCols];
+#pragma unroll
+            for (int c = 0; c < kCols; ++c) tot[c] = 0.f;
+            float s_cur = __half2float(srow[0]);
+            float z_cur = zrow ? (float)((__ldg(zrow) >> zsh) & 0xF) : 8.f;
+            for (int g = 0; g < a.G; ++g, ++it) {
+                const int ss = it % C::kSStages;
+                const int tb = it % C::kAcc;
+                float s_nx = 0.f, z_nx = 8.f;
+                if (g + 1 < a.G) {
+                    s_nx = __half2float(srow[g + 1]);
+                    if (zrow) z_nx = (float)((__ldg(zrow + g + 1) >> zsh) & 0xF);
+                }
+                mbar_wait(&sm.sfull[ss], (it / C::kSStages) & 1, bad);
+                mbar_wait(&sm.tfull[tb], (it / C::kAcc) & 1, bad);
+                __syncwarp();
+                asm volatile("tcgen05.fence::after_thread_sync;" ::);
+                const float2 sv = make_float2(s_cur, s_cur);
+                const float nz = -s_cur * z_cur;
+                const float2 nsz = make_float2(nz, nz);
+                const float* S = &sm.ssum[ss][c0];
+#pragma unroll
+                for (int cc = 0; cc < kCols; cc += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(tb * NT + c0 + cc), v);
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) {
+                        const float4 s4 = *reinterpret_cast<const float4*>(S + cc + j);
+                        float2 t0 = make_float2(tot[cc + j], tot[cc + j + 1]);
+                        float2 t1 = make_float2(tot[cc + j + 2], tot[cc + j + 3]);
+                        t0 = ffma2(nsz, make_float2(s4.x, s4.y), t0);
+                        t1 = ffma2(nsz, make_float2(s4.z, s4.w), t1);
+                        t0 = ffma2(sv, make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1])), t0);
+                        t1 = ffma2(sv, make_float2(__uint_as_float(v[j + 2]), __uint_as_float(v[j + 3])), t1);
+                        tot[cc + j] = t0.x;
+                        tot[cc + j + 1] = t0.y;
+                        tot[cc + j + 2] = t1.x;
+                        tot[cc + j + 3] = t1.y;
+                    }
+                }
+                asm volatile("tcgen05.fence::before_thread_sync;" ::);
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&sm.tempty[tb]);
+                    mbar_arrive(&sm.sempty[ss]);
+                }
+                s_cur = s_nx;
+                z_cur = z_nx;
+            }
+            // ---- epilogue: fp16(tot * a_scale) into the shared tile, then row-contiguous
+            // stores by all fold threads (SiLU(gate) * up for the fused gate_up op) ----
 #pragma unroll
             for (int c = 0; c < kCols; ++c)
-                up[(m - 64) * NT + c0 + c] = __float2half_rn(tot[c] * sm.asc[c0 + c]);
-        __syncthreads();
-        if (!up_row && n_store < n_out)
-#pragma unroll
-            for (int c = 0; c < kCols; ++c) {
-                const int r = r0 + c0 + c;
-                if (r >= P_valid) continue;
-                __half v = __float2half_rn(0.f);
-                if (sm.src[c0 + c] >= 0)
-                    v = silu_and_mul_half(tot[c] * sm.asc[c0 + c],
-                                          __half2float(up[m * NT + c0 + c]));
-                a.out16[(int64_t)r * n_out + n_store] = v;
+                sm.otile[(c0 + c) * 128 + m] = __float2half_rn(
+                    tot[c] * __shfl_sync(0xffffffffu, asc_l[c >> 5], c & 31));
+            asm volatile("bar.sync 1, %0;" ::"n"(kFoldWarps * 32));
+            const int fw = warp - 8;
+            if (a.silu) {
+                const int n = mt * 64 + 2 * lane;  // two outputs per lane
+#pragma unroll 2
+                for (int c = fw; c < NT; c += kFoldWarps) {
+                    const int r = r0 + c;
+                    if (r >= P_valid) break;
+                    const __half2 gh = *reinterpret_cast<const __half2*>(&sm.otile[c * 128 + 2 * lane]);
+                    const __half2 uh = *reinterpret_cast<const __half2*>(&sm.otile[c * 128 + 64 + 2 * lane]);
+                    __half2 o;
+                    o.x = silu_mul_h(__low2half(gh), __low2half(uh));
+                    o.y = silu_mul_h(__high2half(gh), __high2half(uh));
+                    *reinterpret_cast<__half2*>(a.out16 + (int64_t)r * n_out + n) = o;
+                }
+            } else {
+                const int n = mt * 128 + 4 * lane;  // four outputs per lane
+                if (n < n_out)
+#pragma unroll 2
+                    for (int c = fw; c < NT; c += kFoldWarps) {
+                        const int r = r0 + c;
+                        if (r >= P_valid) break;
+                        *reinterpret_cast<uint2*>(a.out16 + (int64_t)r * n_out + n) =
+                            *reinterpret_cast<const uint2*>(&sm.otile[c * 128 + 4 * lane]);
+                    }
             }
-    } else if (n_store < n_out) {
-#pragma unroll
-        for (int c = 0; c < kCols; ++c) {
-            const int r = r0 + c0 + c;
-            if (r >= P_valid) break;
-            const float v = sm.src[c0 + c] >= 0 ? tot[c] * sm.asc[c0 + c] : 0.f;
-            a.out16[(int64_t)r * n_out + n_store] = __float2half_rn(v);
+            asm volatile("bar.sync 1, %0;" ::"n"(kFoldWarps * 32));
         }
     }
-    if (tid == 0 && sm.bad && a.err) atomicOr(a.err, 1);
+
     asm volatile("tcgen05.fence::before_thread_sync;" ::);
     __syncthreads();
-    if (warp == 0) {
+    if (tid == 0 && sm.bad && a.err) atomicOr(a.err, 1);
+    if (warp == 2) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::);
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                     "r"(kTmemCols));
+                     "r"(C::kTmemCols));
     }
+}
+
+// One warp per sorted row: dense sorted-order operand rows for the tile kernel. Rows past the
+// last valid one (up to the tile-rounded count) and rows with a sentinel id are zero-filled.
+__global__ void __launch_bounds__(256) tc_gather_kernel(const TcArgs a, int NT) {
+    const int lane = threadIdx.x & 31;
+    const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int P_valid = a.ntp ? min(a.ntp[0], a.P) : a.P;
+    const int64_t rows = (int64_t)(P_valid + NT - 1) / NT * NT;
+    if (r >= rows) return;
+    int src = -1;
+    if (r < P_valid) {
+        const int e = a.expert_ids ? a.expert_ids[r / a.block_m] : 0;
+        const int sid = a.sorted_ids ? a.sorted_ids[r] : (int)r;
+        if (e >= 0 && e < a.E && sid >= 0 && sid < a.num_valid)
+            src = a.src_identity ? (int)r : sid / a.top_k;
+    }
+    uint4* dst = reinterpret_cast<uint4*>(a.xs + r * a.K);
+    const int64_t nv = a.K / 16;
+    if (src >= 0) {
+        const uint4* sp = reinterpret_cast<const uint4*>(a.xq + (int64_t)src * a.K);
+        for (int64_t i = lane; i < nv; i += 32) dst[i] = __ldg(sp + i);
+        for (int g = lane; g < a.G; g += 32)
+            a.ssum[(int64_t)g * a.P_pad + r] = a.xsum[(int64_t)src * a.G + g].y;
+        if (lane == 0) a.asc_s[r] = a.act_scales[src];
+    } else {
+        for (int64_t i = lane; i < nv; i += 32) dst[i] = make_uint4(0, 0, 0, 0);
+        for (int g = lane; g < a.G; g += 32) a.ssum[(int64_t)g * a.P_pad + r] = 0.f;
+        if (lane == 0) a.asc_s[r] = 0.f;
+    }
+}
+
+// ---- tensor maps ----
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 2D u8 map over rows x row_bytes (row stride row_bytes), box box_bytes x box_rows.
+bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t row_bytes,
+              uint32_t box_bytes, uint32_t box_rows, CUtensorMapSwizzle sw) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {row_bytes, rows};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_bytes, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int sm_count() {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
 }
 
 template <int NT>
 int launch_tc_t(const TcArgs& a, cudaStream_t stream) {
-    const size_t smem = sizeof(TcSmem<NT>) + 128;
+    const int64_t rows_max = (int64_t)(a.P + NT - 1) / NT * NT;
+    tc_gather_kernel<<<(unsigned)((rows_max + 7) / 8), 256, 0, stream>>>(a, NT);
+    if (int rc = launch_status()) return rc;
+    CUtensorMap tmw, tmx;
+    if (!make_map(&tmw, a.w, (uint64_t)a.E * a.N, (uint64_t)a.K / 2, 64, a.silu ? 64 : 128,
+                  CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_map(&tmx, a.xs, (uint64_t)a.P_pad, (uint64_t)a.K, 128, NT,
+                  CU_TENSOR_MAP_SWIZZLE_128B))
+        return set_error("tile path: tensor map encoding failed");
+    const size_t smem = sizeof(TcSmem<NT>) + 1024;
     auto kern = w4_tc_kernel<NT>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return (int)e;
-    const int n_tiles = a.silu ? (a.N / 2) / 64 : (a.N + 127) / 128;
-    const dim3 grid((unsigned)n_tiles, (unsigned)((a.P + NT - 1) / NT));
-    kern<<<grid, kTcThreads, smem, stream>>>(a);
+    const int n_mt = a.silu ? (a.N / 2) / 64 : (a.N + 127) / 128;
+    const int64_t tiles_max = rows_max / NT * n_mt;
+    const int grid = (int)std::min<int64_t>(tiles_max, sm_count());
+    if (grid <= 0) return W4A8_OK;
+    kern<<<grid, kTcThreads, smem, stream>>>(a, tmw, tmx);
     return launch_status();
 }
 
@@ -392,6 +601,24 @@ int launch_tc_t(const TcArgs& a, cudaStream_t stream) {
 bool tc_path_ok(int64_t K, int group_size, int e2m1, const void* w, int block_m) {
     return !e2m1 && group_size == 128 && K % 128 == 0 && K >= 128 &&
            (reinterpret_cast<uintptr_t>(w) & 15) == 0 && block_m % 64 == 0;
+}
+
+size_t tc_scratch_bytes(int64_t P, int64_t K) {
+    const int64_t P_pad = (P + 127) / 128 * 128;
+    const int64_t G = std::max<int64_t>(K / 128, 1);
+    return align_up((size_t)(P_pad * K), 256) + align_up((size_t)P_pad * 4, 256) +
+           align_up((size_t)(G * P_pad) * 4, 256);
+}
+
+void tc_carve(void* base, int64_t P, int64_t K, TcArgs& t) {
+    const int64_t P_pad = (P + 127) / 128 * 128;
+    uint8_t* p = static_cast<uint8_t*>(base);
+    t.xs = p;
+    p += align_up((size_t)(P_pad * K), 256);
+    t.asc_s = reinterpret_cast<float*>(p);
+    p += align_up((size_t)P_pad * 4, 256);
+    t.ssum = reinterpret_cast<float*>(p);
+    t.P_pad = (int)P_pad;
 }
 
 int launch_w4_tc(TcArgs a, cudaStream_t stream) {
