@@ -191,6 +191,16 @@ W4A8_API int w4a8_moe_gather_reduce(const void* out2, const int32_t* sorted_toke
                            void* workspace, size_t workspace_bytes, w4a8_stream_t stream);
 
 /*
+ * silu_and_mul on fp16 rows: x (M, 2*inter) [gate | up] -> out (M, inter),
+ * out = fp16(g / (1 + expf(-g))) * up with g the fp16 gate (IEEE divide, half*half product).
+ * The unfused composition's activation step between gate_up and down, which the reference
+ * takes from vLLM (apply_moe_activation, w4a8_fp8_wmma/w4a8_fp8_wmma/moe_experts.py:620-630);
+ * the fused gate_up op applies the same arithmetic in its epilogue.
+ */
+W4A8_API int w4a8_silu_and_mul(const void* x, void* out, int64_t M, int64_t inter,
+                               w4a8_stream_t stream);
+
+/*
  * Whole gated MoE layer at decode sizes in one call: moe_align (block 8) -> gate_up GEMV ->
  * silu_and_mul -> down GEMV -> topk-weighted reduce, the decode branch of the reference's
  * composition _run_grouped_moe (w4a8_fp8_wmma/w4a8_fp8_wmma/moe_experts.py:563-648), which

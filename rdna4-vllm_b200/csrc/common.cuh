@@ -93,9 +93,22 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
 // evaluated in fp32 and rounded to fp16, the product is a half*half multiply (the reference's
 // moe_silu_and_mul_h, w4a8_fp8_wmma/moe_kernel.hip:555-565; oracle test_moe_experts.py:274-280).
 // The same on operands already rounded to fp16.
+//
+// fp16(g / d) is taken from the fast quotient g * rcp(d) (div.approx: within 2 ulp of the
+// IEEE quotient for the d that occur here, 1 <= d < 2^126) whenever the whole interval
+// quotient * (1 -/+ 2^-20) rounds to one fp16 value: the IEEE quotient lies inside it and
+// rounding is monotonic, so that value is exactly fp16(IEEE quotient). Otherwise (a quotient
+// within a few fp32 ulp of an fp16 rounding boundary, about 0.1% of inputs) the IEEE divide
+// decides. The result equals fp16(g / (1 + expf(-g))) with an IEEE divide, bit for bit.
 __device__ __forceinline__ __half silu_mul_h(__half gh, __half uh) {
     const float g = __half2float(gh);
-    const __half sh = __float2half_rn(__fdiv_rn(g, 1.0f + expf(-g)));
+    const float d = 1.0f + expf(-g);
+    const float qa = __fdividef(g, d);
+    const float w = fabsf(qa) * 0x1p-20f;
+    __half sh = __float2half_rn(qa);
+    if (__half_as_ushort(__float2half_rn(qa - w)) != __half_as_ushort(__float2half_rn(qa + w)) ||
+        !(d < 0x1p126f))
+        sh = __float2half_rn(__fdiv_rn(g, d));
     return __hmul(sh, uh);
 }
 __device__ __forceinline__ __half silu_and_mul_half(float gate_f, float up_f) {

@@ -10,14 +10,19 @@
 //      the (tile, K-group) steps flow through mbarrier rings, so the next tile's loads and MMAs
 //      overlap the current tile's epilogue.
 //
-// Roles (16 warps):
+// Roles (16 warps). In the expansion and fold roles one leader thread waits on the mbarriers
+// and a named barrier releases the role's other warps.
 //   warp 0      TMA producer: weight codes (2D box, 64-byte swizzle), token tile (2D box,
 //               128-byte swizzle = the UMMA K-major SW128 layout), group sums (bulk copy).
-//   warp 1      MMA issuer: 4 x tcgen05.mma.kind::f8f6f4 (K = 32 each) per group into one of the
-//               TMEM accumulators (512 columns / NT), committed to the stage / A / accumulator barriers.
-//   warp 2      owns the tensor-memory allocation.
-//   warps 4-7   expand the 4-bit codes to e4m3 bytes in the SW128 A layout (thread = weight row).
-//   warps 8-15  fold each group's accumulator into fp32 registers and write the tile's output.
+//   warp 1      MMA issuer: 4 x tcgen05.mma.kind::f8f6f4 (K = 32 each) per group, A from tensor
+//               memory, B from shared memory, into one of the TMEM accumulators, committed to
+//               the stage / A / accumulator barriers.
+//   warp 2      owns the tensor-memory allocation; loads each group's weight scales and zeros
+//               into a shared ring as {s, -s*z}.
+//   warps 4-7   expand the 4-bit codes to e4m3 bytes and store them to the A tile in tensor
+//               memory (thread = weight row = TMEM lane).
+//   warps 8-15  fold each group's accumulator into fp32 registers (4 lane quadrants x 2 column
+//               halves) and write the finished tiles' outputs.
 //
 // Numerics. The A operand holds e4m3(q) — the unsigned 4-bit code itself, exact in e4m3 — so
 // per 128-wide group g the tensor core returns acc = sum_k q_k a_k. With S_g = sum_k a_k the
@@ -43,16 +48,22 @@ namespace w4a8 {
 
 namespace {
 
+#ifndef W4A8_TC_DEFER
+#define W4A8_TC_DEFER 0
+#endif
 constexpr int kTcThreads = 512;
-constexpr uint32_t kSpinLimit = 1u << 22;
+constexpr uint64_t kWaitLimitNs = 1000000000ull;   // a wait gives up after 1 s
 constexpr int kFoldWarps = 8;
 
 template <int NT>
 struct TcCfg {
-    static constexpr int kStages = NT == 128 ? 5 : 7;  // TMA ring depth (codes + tokens)
-    static constexpr int kAStages = NT == 128 ? 4 : 5; // dequantised-A ring depth
+    static constexpr int kStages = NT == 128 ? 6 : 11; // TMA ring depth (codes + tokens)
     static constexpr int kSStages = 8;                 // group-sum ring depth
-    static constexpr int kAcc = 512 / NT;              // TMEM accumulators (all 512 columns)
+    // Tensor memory (512 columns): kAcc fp32 accumulators of NT columns, then kAStages
+    // dequantised A tiles of 32 columns (128 rows x 128 e4m3 bytes each).
+    static constexpr int kAcc = NT == 128 ? 3 : 4;
+    static constexpr int kAStages = (512 - kAcc * NT) / 32;
+    static constexpr uint32_t kACol0 = kAcc * NT;
     static constexpr int kCols = NT / 2;               // accumulator columns per fold thread
     static constexpr uint32_t kTmemCols = 512;
     static constexpr uint32_t kStageBytes = 128 * 64 + NT * 128;
@@ -61,10 +72,10 @@ struct TcCfg {
 template <int NT>
 struct TcSmem {
     uint8_t b[TcCfg<NT>::kStages][NT * 128];     // token tiles, SW128 K-major (1024-aligned)
-    uint8_t a[TcCfg<NT>::kAStages][128 * 128];   // e4m3 weights, SW128 K-major
     uint8_t raw[TcCfg<NT>::kStages][128 * 64];   // packed codes, SW64 as TMA writes them
-    __half otile[NT * 128];                      // epilogue: fp16 results, [column][row]
+    __half otile[2][NT * 128];                   // finished tiles, fp16, [column][row]
     float ssum[TcCfg<NT>::kSStages][NT];         // group sums S of the tile's rows
+    float2 meta[TcCfg<NT>::kSStages][128];       // per weight row: {scale, -scale * zero}
     uint64_t full[TcCfg<NT>::kStages];
     uint64_t empty[TcCfg<NT>::kStages];
     uint64_t sfull[TcCfg<NT>::kSStages];
@@ -122,12 +133,28 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
         : "memory");
     return done != 0;
 }
-// Bounded wait; once any wait in the CTA has given up, later waits return at once.
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait: try_wait in a loop (the instruction itself suspends the thread for a short,
+// hardware-defined time), giving up after kWaitLimitNs; once any wait in the CTA has given up,
+// later waits return at once.
 __device__ __forceinline__ void mbar_wait(uint64_t* bar, uint32_t parity, volatile int* bad) {
+    if (mbar_try(bar, parity)) return;
     if (*bad) return;
-    for (uint32_t i = 0; i < kSpinLimit; ++i)
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 1;; ++i) {
         if (mbar_try(bar, parity)) return;
-    *bad = 1;
+        if ((i & 255) == 0) {
+            if (*bad) return;
+            if (global_ns() - t0 > kWaitLimitNs) {
+                *bad = 1;
+                return;
+            }
+        }
+    }
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
@@ -152,18 +179,18 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
         : "memory");
 }
 
-// 4 codes (the low 16 bits of `w`, nibble i = code i) -> 4 e4m3 bytes of the codes' values.
-// Bytes of codes 0..7 come from the table {0, 1, 2, 3, 4, 5, 6, 7} in e4m3; codes 8..15 are
-// 0x50 + (q - 8) (exponent 3, mantissa q - 8). prmt's sign-replicate mode (selector bit 3)
-// turns the high codes into 0x00 in the first lookup and into an all-ones mask in the third.
-__device__ __forceinline__ uint32_t codes_to_e4m3(uint32_t w) {
+// 8 codes (nibble i of `w` = code i) -> 8 e4m3 bytes of the codes' values, codes 0..3 in `lo`
+// and 4..7 in `hi`. prmt looks up 4 bytes at once from the selector's low 4 nibbles; a nibble
+// with bit 3 set selects in sign-replicate mode, which yields 0x00 for the positive table
+// bytes used here. The first lookup (selector = code) gives e4m3(q) for q < 8 and 0 for
+// q >= 8; the second (selector = code ^ 8) gives e4m3(q) = 0x50 + (q - 8) for q >= 8 and 0 for
+// q < 8; their OR is e4m3(q) for every code.
+__device__ __forceinline__ void codes8_to_e4m3(uint32_t w, uint32_t& lo, uint32_t& hi) {
     constexpr uint32_t kLo0 = 0x44403800u, kLo1 = 0x4E4C4A48u;  // e4m3(0..7)
     constexpr uint32_t kHi0 = 0x53525150u, kHi1 = 0x57565554u;  // e4m3(8..15)
-    constexpr uint32_t kSign = 0x80808080u;
-    const uint32_t lo = prmt(kLo0, kLo1, w);                // q<8: e4m3(q); q>=8: 0x00
-    const uint32_t hi = prmt(kHi0, kHi1, w & 0x7777u);      // e4m3(8 + (q & 7))
-    const uint32_t m = prmt(kSign, kSign, w);               // q<8: 0x80; q>=8: 0xFF
-    return lop3<(0xF0 & 0xCC) | (~0xF0 & 0xAA)>(m, hi, lo); // m ? hi : lo, bitwise
+    const uint32_t wx = w ^ 0x88888888u;
+    lo = prmt(kLo0, kLo1, w) | prmt(kHi0, kHi1, wx);
+    hi = prmt(kLo0, kLo1, w >> 16) | prmt(kHi0, kHi1, wx >> 16);
 }
 
 // d = a * b + c on two fp32 lanes at once.
@@ -176,7 +203,23 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
     return *reinterpret_cast<float2*>(&d);
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&v)[N]);
+
+template <>
+__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,"
+        "%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+          "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
+          "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+template <>
+__device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, uint32_t (&v)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,"
         "%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31},"
@@ -191,11 +234,52 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Expert of tile row block rb (0 for the dense GEMM).
-__device__ __forceinline__ int tile_expert(const TcArgs& a, int rb, int NT) {
-    if (!a.expert_ids) return 0;
-    return a.expert_ids[(int64_t)rb * NT / a.block_m];
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+        "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+        "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
+        "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
+        "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
 }
+
+
+// Stage index + phase bit of a barrier ring, advanced one step per K group.
+template <int N>
+struct RingPos {
+    uint32_t idx = 0, phase = 0;
+    __device__ __forceinline__ void next() {
+        if (++idx == N) {
+            idx = 0;
+            phase ^= 1;
+        }
+    }
+};
+
+// The tile sequence of one CTA: t = blockIdx.x + i * gridDim.x, t = rb * n_mt + mt, walked
+// without per-step division. `expert` is the tile's expert (0 for the dense GEMM).
+struct TileWalk {
+    int rb, mt, drb, dmt, n_mt, nblk, bpe;
+    __device__ __forceinline__ TileWalk(int n_mt_, int nblk_, int bpe_)
+        : rb(blockIdx.x / n_mt_), mt(blockIdx.x % n_mt_), drb(gridDim.x / n_mt_),
+          dmt(gridDim.x % n_mt_), n_mt(n_mt_), nblk(nblk_), bpe(bpe_) {}
+    __device__ __forceinline__ bool more() const { return rb < nblk; }
+    __device__ __forceinline__ void next() {
+        rb += drb;
+        mt += dmt;
+        if (mt >= n_mt) {
+            mt -= n_mt;
+            ++rb;
+        }
+    }
+    __device__ __forceinline__ int expert(const TcArgs& a) const {
+        return a.expert_ids ? a.expert_ids[rb / bpe] : 0;
+    }
+};
 
 template <int NT>
 __global__ void __launch_bounds__(kTcThreads, 1)
@@ -211,8 +295,9 @@ w4_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmw,
     const int P_valid = a.ntp ? min(a.ntp[0], a.P) : a.P;
     const int nblk = (P_valid + NT - 1) / NT;
     const int n_mt = a.silu ? (a.N / 2) / 64 : (a.N + 127) / 128;
-    const int n_tiles = nblk * n_mt;
     const int n_out = a.silu ? a.N / 2 : a.N;
+    const int bpe = a.expert_ids ? a.block_m / NT : 1;  // tile row blocks per expert block
+    const int G = a.G;
 
     if (tid == 0) {
         sm.bad = 0;
@@ -221,7 +306,7 @@ w4_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmw,
             mbar_init(&sm.empty[s], 1);
         }
         for (int s = 0; s < C::kSStages; ++s) {
-            mbar_init(&sm.sfull[s], 1);
+            mbar_init(&sm.sfull[s], 1 + 32);  // producer's bulk copy + the meta warp's lanes
             mbar_init(&sm.sempty[s], kFoldWarps);
         }
         for (int s = 0; s < C::kAStages; ++s) {
@@ -248,165 +333,273 @@ w4_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmw,
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
-            uint32_t it = 0;
-            for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
-                const int rb = t / n_mt, mt = t % n_mt;
-                const int e = tile_expert(a, rb, NT);
+            RingPos<C::kStages> st;
+            RingPos<C::kSStages> ss;
+            uint32_t issued = 0;
+            for (TileWalk tw(n_mt, nblk, bpe); tw.more(); tw.next()) {
+                const int e = tw.expert(a);
                 if (e < 0 || e >= a.E) continue;
-                const int r0 = rb * NT;
+                const int r0 = tw.rb * NT, mt = tw.mt;
                 // warm L2 with this CTA's next tile (weights and tokens) while this one runs
-                const int tn = t + gridDim.x;
-                if (tn < n_tiles) {
-                    const int rbn = tn / n_mt, mtn = tn % n_mt;
-                    const int en = tile_expert(a, rbn, NT);
+                TileWalk nx = tw;
+                nx.next();
+                if (nx.more()) {
+                    const int en = nx.expert(a);
                     if (en >= 0 && en < a.E)
-                        for (int g = 0; g < a.G; ++g) {
+                        for (int g = 0; g < G; ++g) {
                             if (a.silu) {
-                                tma_prefetch_2d(&tmw, g * 64, en * a.N + mtn * 64);
-                                tma_prefetch_2d(&tmw, g * 64, en * a.N + a.N / 2 + mtn * 64);
+                                tma_prefetch_2d(&tmw, g * 64, en * a.N + nx.mt * 64);
+                                tma_prefetch_2d(&tmw, g * 64, en * a.N + a.N / 2 + nx.mt * 64);
                             } else {
-                                tma_prefetch_2d(&tmw, g * 64, en * a.N + mtn * 128);
+                                tma_prefetch_2d(&tmw, g * 64, en * a.N + nx.mt * 128);
                             }
-                            tma_prefetch_2d(&tmx, g * 128, rbn * NT);
+                            tma_prefetch_2d(&tmx, g * 128, nx.rb * NT);
                         }
                 }
-                for (int g = 0; g < a.G; ++g, ++it) {
-                    const int s = it % C::kStages;
-                    const int ss = it % C::kSStages;
-                    mbar_wait(&sm.empty[s], ((it / C::kStages) & 1) ^ 1, bad);
-                    mbar_expect_tx(&sm.full[s], C::kStageBytes);
+                for (int g = 0; g < G; ++g) {
+                    uint64_t* fb = &sm.full[st.idx];
+                    mbar_wait(&sm.empty[st.idx], st.phase ^ 1, bad);
+                    mbar_expect_tx(fb, C::kStageBytes);
+                    uint8_t* raw = &sm.raw[st.idx][0];
                     if (a.silu) {
-                        tma_load_2d(&sm.raw[s][0], &tmw, g * 64, e * a.N + mt * 64, &sm.full[s]);
-                        tma_load_2d(&sm.raw[s][64 * 64], &tmw, g * 64,
-                                    e * a.N + a.N / 2 + mt * 64, &sm.full[s]);
+                        tma_load_2d(raw, &tmw, g * 64, e * a.N + mt * 64, fb);
+                        tma_load_2d(raw + 64 * 64, &tmw, g * 64, e * a.N + a.N / 2 + mt * 64, fb);
                     } else {
-                        tma_load_2d(&sm.raw[s][0], &tmw, g * 64, e * a.N + mt * 128, &sm.full[s]);
+                        tma_load_2d(raw, &tmw, g * 64, e * a.N + mt * 128, fb);
                     }
-                    tma_load_2d(&sm.b[s][0], &tmx, g * 128, r0, &sm.full[s]);
-                    mbar_wait(&sm.sempty[ss], ((it / C::kSStages) & 1) ^ 1, bad);
-                    mbar_expect_tx(&sm.sfull[ss], NT * 4);
-                    bulk_load(&sm.ssum[ss][0], a.ssum + (int64_t)g * a.P_pad + r0, NT * 4,
-                              &sm.sfull[ss]);
+                    tma_load_2d(&sm.b[st.idx][0], &tmx, g * 128, r0, fb);
+                    mbar_wait(&sm.sempty[ss.idx], ss.phase ^ 1, bad);
+                    mbar_expect_tx(&sm.sfull[ss.idx], NT * 4);
+                    bulk_load(&sm.ssum[ss.idx][0], a.ssum + (int64_t)g * a.P_pad + r0, NT * 4,
+                              &sm.sfull[ss.idx]);
+                    st.next();
+                    ss.next();
+                    ++issued;
                 }
             }
             // leave no copy in flight: wait (boundedly) for the last ring's worth of loads
             if (*bad) {
-                const uint32_t first = it > (uint32_t)C::kStages ? it - C::kStages : 0;
-                for (uint32_t j = first; j < it; ++j)
-                    for (uint32_t i = 0; i < kSpinLimit; ++i)
-                        if (mbar_try(&sm.full[j % C::kStages], (j / C::kStages) & 1)) break;
-                const uint32_t sfirst = it > (uint32_t)C::kSStages ? it - C::kSStages : 0;
-                for (uint32_t j = sfirst; j < it; ++j)
-                    for (uint32_t i = 0; i < kSpinLimit; ++i)
-                        if (mbar_try(&sm.sfull[j % C::kSStages], (j / C::kSStages) & 1)) break;
+                const uint64_t t0 = global_ns();
+                for (uint32_t j = 0; j < (uint32_t)C::kStages && j < issued; ++j)
+                    while (!mbar_try(&sm.full[j], ((issued - 1 - j) / C::kStages) & 1) &&
+                           global_ns() - t0 < kWaitLimitNs) {
+                    }
+                for (uint32_t j = 0; j < (uint32_t)C::kSStages && j < issued; ++j)
+                    while (!mbar_try(&sm.sfull[j], ((issued - 1 - j) / C::kSStages) & 1) &&
+                           global_ns() - t0 < kWaitLimitNs) {
+                    }
             }
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             constexpr uint32_t idesc = umma_idesc(128, NT);
-            uint32_t it = 0;
-            for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
-                const int e = tile_expert(a, t / n_mt, NT);
+            RingPos<C::kStages> st;
+            RingPos<C::kAStages> as;
+            RingPos<C::kAcc> tb;
+            for (TileWalk tw(n_mt, nblk, bpe); tw.more(); tw.next()) {
+                const int e = tw.expert(a);
                 if (e < 0 || e >= a.E) continue;
-                for (int g = 0; g < a.G; ++g, ++it) {
-                    const int s = it % C::kStages;
-                    const int as = it % C::kAStages;
-                    const int tb = it % C::kAcc;
-                    mbar_wait(&sm.full[s], (it / C::kStages) & 1, bad);
-                    mbar_wait(&sm.afull[as], (it / C::kAStages) & 1, bad);
-                    mbar_wait(&sm.tempty[tb], ((it / C::kAcc) & 1) ^ 1, bad);
+                for (int g = 0; g < G; ++g) {
+                    mbar_wait(&sm.full[st.idx], st.phase, bad);
+                    mbar_wait(&sm.afull[as.idx], as.phase, bad);
+                    mbar_wait(&sm.tempty[tb.idx], tb.phase ^ 1, bad);
                     asm volatile("tcgen05.fence::after_thread_sync;" ::);
-                    const uint32_t a0 = smem_u32(&sm.a[as][0]);
-                    const uint32_t b0 = smem_u32(&sm.b[s][0]);
-                    const uint32_t d = tmem + (uint32_t)(tb * NT);
+                    const uint32_t ta = tmem + C::kACol0 + as.idx * 32;
+                    const uint32_t b0 = smem_u32(&sm.b[st.idx][0]);
+                    const uint32_t d = tmem + tb.idx * NT;
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        const uint64_t da = desc_sw128(a0 + kk * 32);
+                    for (int kk = 0; kk < 4; ++kk) {  // K = 32 e4m3 = 8 TMEM columns of A
                         const uint64_t db = desc_sw128(b0 + kk * 32);
                         const uint32_t acc = kk > 0 ? 1u : 0u;
                         asm volatile(
                             "{\n\t.reg .pred p;\n\t"
                             "setp.ne.b32 p, %4, 0;\n\t"
-                            "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
-                            "l"(da), "l"(db), "r"(idesc), "r"(acc));
+                            "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+                            "r"(ta + kk * 8), "l"(db), "r"(idesc), "r"(acc));
                     }
                     asm volatile(
                         "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                        ::"r"(smem_u32(&sm.empty[s])));
+                        ::"r"(smem_u32(&sm.empty[st.idx])));
                     asm volatile(
                         "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                        ::"r"(smem_u32(&sm.aempty[as])));
+                        ::"r"(smem_u32(&sm.aempty[as.idx])));
                     asm volatile(
                         "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                        ::"r"(smem_u32(&sm.tfull[tb])));
+                        ::"r"(smem_u32(&sm.tfull[tb.idx])));
+                    st.next();
+                    as.next();
+                    tb.next();
                 }
             }
         }
-    } else if (warp >= 4 && warp < 8) {
-        // ---------------- code expansion: thread = weight row ----------------
-        const int m = tid - 128;
-        const int sw64 = (m >> 1) & 3, sw128 = m & 7;
-        uint32_t it = 0;
-        for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
-            const int e = tile_expert(a, t / n_mt, NT);
-            if (e < 0 || e >= a.E) continue;
-            for (int g = 0; g < a.G; ++g, ++it) {
-                const int s = it % C::kStages;
-                const int as = it % C::kAStages;
-                mbar_wait(&sm.full[s], (it / C::kStages) & 1, bad);
-                mbar_wait(&sm.aempty[as], ((it / C::kAStages) & 1) ^ 1, bad);
-                const uint8_t* rr = &sm.raw[s][m * 64];
-                uint8_t* ar = &sm.a[as][m * 128];
+    } else if (warp == 2) {
+        // ---------------- per-row group scales / zeros -> {s, -s*z} ----------------
+        // Lane l serves rows l, l+32, l+64, l+96. Loads run one chunk of up to 4 groups ahead
+        // of the stores, so their latency hides behind the fold of the previous chunk.
+        const int cg = (G % 4 == 0) ? 4 : 1;
+        RingPos<C::kSStages> ss;
+        TileWalk tw(n_mt, nblk, bpe);
+        auto skip_invalid = [&](TileWalk& w) {
+            while (w.more()) {
+                const int e = w.expert(a);
+                if (e >= 0 && e < a.E) break;
+                w.next();
+            }
+        };
+        skip_invalid(tw);
+        float sc[4][4], sn[4][4];  // current / next chunk: [row][group]
+        int zc[4][4], zn[4][4];
+        auto load = [&](float (&sd)[4][4], int (&zd)[4][4], const TileWalk& w, int gg) {
+            const int e = w.expert(a);
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {  // 32 codes -> two 16-byte e4m3 chunks
-                    const uint4 w = *reinterpret_cast<const uint4*>(rr + ((j ^ sw64) << 4));
-                    uint4 o0, o1;
-                    o0.x = codes_to_e4m3(w.x);
-                    o0.y = codes_to_e4m3(w.x >> 16);
-                    o0.z = codes_to_e4m3(w.y);
-                    o0.w = codes_to_e4m3(w.y >> 16);
-                    o1.x = codes_to_e4m3(w.z);
-                    o1.y = codes_to_e4m3(w.z >> 16);
-                    o1.z = codes_to_e4m3(w.w);
-                    o1.w = codes_to_e4m3(w.w >> 16);
-                    *reinterpret_cast<uint4*>(ar + (((2 * j) ^ sw128) << 4)) = o0;
-                    *reinterpret_cast<uint4*>(ar + (((2 * j + 1) ^ sw128) << 4)) = o1;
+            for (int r = 0; r < 4; ++r) {
+                const int m = lane + 32 * r;
+                int n;
+                if (a.silu) n = m >= 64 ? a.N / 2 + w.mt * 64 + (m - 64) : w.mt * 64 + m;
+                else n = w.mt * 128 + m;
+                const int nn = n < a.N ? n : 0;
+                const __half* sp = a.scales + ((int64_t)e * a.N + nn) * G + gg;
+                const int32_t* zp =
+                    a.zeros ? a.zeros + ((int64_t)e * (a.N / 8) + (nn >> 3)) * G + gg : nullptr;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    if (j < cg) {
+                        sd[r][j] = __half2float(sp[j]);
+                        zd[r][j] = zp ? ((__ldg(zp + j) >> ((nn & 7) * 4)) & 0xF) : 8;
+                    }
                 }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            }
+        };
+        int g0 = 0;
+        if (tw.more()) load(sc, zc, tw, 0);
+        while (tw.more()) {
+            TileWalk wn = tw;  // next chunk's coordinates, then its loads
+            int gn = g0 + cg;
+            if (gn >= G) {
+                gn = 0;
+                wn.next();
+                skip_invalid(wn);
+            }
+            if (wn.more()) load(sn, zn, wn, gn);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (j < cg) {
+                    if (lane == 0) mbar_wait(&sm.sempty[ss.idx], ss.phase ^ 1, bad);
+                    __syncwarp();
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        const float sv = sc[r][j];
+                        sm.meta[ss.idx][lane + 32 * r] = make_float2(sv, -sv * (float)zc[r][j]);
+                    }
+                    mbar_arrive(&sm.sfull[ss.idx]);
+                    ss.next();
+                }
+            }
+            tw = wn;
+            g0 = gn;
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    sc[r][j] = sn[r][j];
+                    zc[r][j] = zn[r][j];
+                }
+        }
+    } else if (warp >= 4 && warp < 8) {
+        // ---------------- code expansion: thread = weight row = TMEM lane ----------------
+        // Warp 4's lane 0 waits for the stage and the A slot; a named barrier releases the rest.
+        const int m = tid - 128;
+        const int sw64 = (m >> 1) & 3;
+        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+        RingPos<C::kStages> st;
+        RingPos<C::kAStages> as;
+        for (TileWalk tw(n_mt, nblk, bpe); tw.more(); tw.next()) {
+            const int e = tw.expert(a);
+            if (e < 0 || e >= a.E) continue;
+            for (int g = 0; g < G; ++g) {
+                if (tid == 128) {
+                    mbar_wait(&sm.full[st.idx], st.phase, bad);
+                    mbar_wait(&sm.aempty[as.idx], as.phase ^ 1, bad);
+                }
+                asm volatile("bar.sync 2, 128;" ::: "memory");
+                // row m of the A tile = TMEM lane m; column j holds e4m3 bytes k = 4j..4j+3
+                const uint8_t* rr = &sm.raw[st.idx][m * 64];
+                uint32_t o[32];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {  // 16 raw bytes = 32 codes = 8 TMEM columns
+                    const uint4 w = *reinterpret_cast<const uint4*>(rr + ((j ^ sw64) << 4));
+                    codes8_to_e4m3(w.x, o[8 * j + 0], o[8 * j + 1]);
+                    codes8_to_e4m3(w.y, o[8 * j + 2], o[8 * j + 3]);
+                    codes8_to_e4m3(w.z, o[8 * j + 4], o[8 * j + 5]);
+                    codes8_to_e4m3(w.w, o[8 * j + 6], o[8 * j + 7]);
+                }
+                tmem_st32(tmem + lane_base + C::kACol0 + as.idx * 32, o);
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                asm volatile("tcgen05.fence::before_thread_sync;" ::);
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&sm.afull[as]);
+                if (lane == 0) mbar_arrive(&sm.afull[as.idx]);
+                st.next();
+                as.next();
             }
         }
     } else if (warp >= 8) {
-        // ---------------- fold + epilogue ----------------
+        // ---------------- fold + deferred epilogue ----------------
+        // Warp w folds TMEM lane quadrant w % 4, columns [h * kCols, (h + 1) * kCols). Warp 8's
+        // lane 0 waits for the group's sums and accumulator; a named barrier releases the rest.
+        // A finished tile goes to a shared fp16 tile (double buffered); its SiLU / stores are
+        // spread over the K-groups of the CTA's next tile (slice g of G per group), where they
+        // fill the fold warps' waits, and flushed after the last tile.
         constexpr int kCols = C::kCols;
-        const int q = warp & 3;                     // TMEM lane quadrant
-        const int c0 = ((warp - 8) >> 2) * kCols;   // column half
-        const int m = q * 32 + lane;                // tile row = TMEM lane
-        const bool up_row = a.silu && m >= 64;
-        uint32_t it = 0;
-        for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
-            const int rb = t / n_mt, mt = t % n_mt;
-            const int e = tile_expert(a, rb, NT);
-            const int r0 = rb * NT;
-            int n;
-            if (a.silu) n = up_row ? a.N / 2 + mt * 64 + (m - 64) : mt * 64 + m;
-            else n = mt * 128 + m;
-            const int n_store = a.silu ? mt * 64 + (m & 63) : n;
-            if (e < 0 || e >= a.E) {  // non-local expert: zeros
-                if (!up_row && n_store < n_out)
-#pragma unroll 4
-                    for (int c = 0; c < kCols; ++c)
-                        if (r0 + c0 + c < P_valid)
-                            a.out16[(int64_t)(r0 + c0 + c) * n_out + n_store] = __float2half_rn(0.f);
+        const int q = warp & 3;
+        const int fw = warp - 8;
+        const int c0 = (fw >> 2) * kCols;
+        const int m = q * 32 + lane;  // tile row = TMEM lane
+        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        RingPos<C::kSStages> ss;
+        RingPos<C::kAcc> tb;
+        int pend_buf = -1, pend_r0 = 0, pend_mt = 0, tiles_done = 0;
+        // columns [c_lo, c_hi) of the pending tile: SiLU(gate) * up, or a copy, to global
+        auto drain = [&](int c_lo, int c_hi) {
+            const __half* ot = sm.otile[pend_buf];
+            if (a.silu) {
+                const int n = pend_mt * 64 + 2 * lane;
+                for (int c = c_lo + fw; c < c_hi; c += kFoldWarps) {
+                    const int r = pend_r0 + c;
+                    if (r >= P_valid) break;
+                    const __half2 gh = *reinterpret_cast<const __half2*>(&ot[c * 128 + 2 * lane]);
+                    const __half2 uh = *reinterpret_cast<const __half2*>(&ot[c * 128 + 64 + 2 * lane]);
+                    __half2 o;
+                    o.x = silu_mul_h(__low2half(gh), __low2half(uh));
+                    o.y = silu_mul_h(__high2half(gh), __high2half(uh));
+                    *reinterpret_cast<__half2*>(a.out16 + (int64_t)r * n_out + n) = o;
+                }
+            } else {
+                const int n = pend_mt * 128 + 4 * lane;
+                if (n < n_out)
+                    for (int c = c_lo + fw; c < c_hi; c += kFoldWarps) {
+                        const int r = pend_r0 + c;
+                        if (r >= P_valid) break;
+                        *reinterpret_cast<uint2*>(a.out16 + (int64_t)r * n_out + n) =
+                            *reinterpret_cast<const uint2*>(&ot[c * 128 + 4 * lane]);
+                    }
+            }
+        };
+        for (TileWalk tw(n_mt, nblk, bpe); tw.more(); tw.next()) {
+            const int e = tw.expert(a);
+            const int r0 = tw.rb * NT, mt = tw.mt;
+            if (e < 0 || e >= a.E) {  // non-local expert: zero rows
+                const int n = a.silu ? mt * 64 + 2 * lane : mt * 128 + 4 * lane;
+                for (int c = fw; c < NT; c += kFoldWarps) {
+                    const int r = r0 + c;
+                    if (r >= P_valid) break;
+                    if (a.silu)
+                        *reinterpret_cast<uint32_t*>(a.out16 + (int64_t)r * n_out + n) = 0u;
+                    else if (n < n_out)
+                        *reinterpret_cast<uint2*>(a.out16 + (int64_t)r * n_out + n) = make_uint2(0u, 0u);
+                }
                 continue;
             }
-            const int nn = n < a.N ? n : 0;
-            const __half* srow = a.scales + ((int64_t)e * a.N + nn) * a.G;
-            const int32_t* zrow =
-                a.zeros ? a.zeros + ((int64_t)e * (a.N / 8) + (nn >> 3)) * a.G : nullptr;
-            const int zsh = (nn & 7) * 4;
             // activation scales of the tile's columns: lane l holds columns c0 + l (+ 32)
             float asc_l[kCols / 32];
 #pragma unroll
@@ -414,28 +607,21 @@ w4_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmw,
             float tot[kCols];
 #pragma unroll
             for (int c = 0; c < kCols; ++c) tot[c] = 0.f;
-            float s_cur = __half2float(srow[0]);
-            float z_cur = zrow ? (float)((__ldg(zrow) >> zsh) & 0xF) : 8.f;
-            for (int g = 0; g < a.G; ++g, ++it) {
-                const int ss = it % C::kSStages;
-                const int tb = it % C::kAcc;
-                float s_nx = 0.f, z_nx = 8.f;
-                if (g + 1 < a.G) {
-                    s_nx = __half2float(srow[g + 1]);
-                    if (zrow) z_nx = (float)((__ldg(zrow + g + 1) >> zsh) & 0xF);
+            for (int g = 0; g < G; ++g) {
+                if (tid == 256) {
+                    mbar_wait(&sm.sfull[ss.idx], ss.phase, bad);
+                    mbar_wait(&sm.tfull[tb.idx], tb.phase, bad);
                 }
-                mbar_wait(&sm.sfull[ss], (it / C::kSStages) & 1, bad);
-                mbar_wait(&sm.tfull[tb], (it / C::kAcc) & 1, bad);
-                __syncwarp();
+                asm volatile("bar.sync 3, %0;" ::"n"(kFoldWarps * 32) : "memory");
                 asm volatile("tcgen05.fence::after_thread_sync;" ::);
-                const float2 sv = make_float2(s_cur, s_cur);
-                const float nz = -s_cur * z_cur;
-                const float2 nsz = make_float2(nz, nz);
-                const float* S = &sm.ssum[ss][c0];
+                const float2 md = sm.meta[ss.idx][m];
+                const float2 sv = make_float2(md.x, md.x);
+                const float2 nsz = make_float2(md.y, md.y);
+                const float* S = &sm.ssum[ss.idx][c0];
 #pragma unroll
                 for (int cc = 0; cc < kCols; cc += 32) {
                     uint32_t v[32];
-                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(tb * NT + c0 + cc), v);
+                    tmem_ld<32>(tmem + lane_base + tb.idx * NT + c0 + cc, v);
 #pragma unroll
                     for (int j = 0; j < 32; j += 4) {
                         const float4 s4 = *reinterpret_cast<const float4*>(S + cc + j);
@@ -454,46 +640,32 @@ w4_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmw,
                 asm volatile("tcgen05.fence::before_thread_sync;" ::);
                 __syncwarp();
                 if (lane == 0) {
-                    mbar_arrive(&sm.tempty[tb]);
-                    mbar_arrive(&sm.sempty[ss]);
+                    mbar_arrive(&sm.tempty[tb.idx]);
+                    mbar_arrive(&sm.sempty[ss.idx]);
                 }
-                s_cur = s_nx;
-                z_cur = z_nx;
+                ss.next();
+                tb.next();
+#if W4A8_TC_DEFER
+                if (pend_buf >= 0) drain(g * NT / G, (g + 1) * NT / G);
+#endif
             }
-            // ---- epilogue: fp16(tot * a_scale) into the shared tile, then row-contiguous
-            // stores by all fold threads (SiLU(gate) * up for the fused gate_up op) ----
+            // park the finished tile: fp16(tot * a_scale) into the free shared tile
+            const int buf = tiles_done & 1;
 #pragma unroll
             for (int c = 0; c < kCols; ++c)
-                sm.otile[(c0 + c) * 128 + m] = __float2half_rn(
+                sm.otile[buf][(c0 + c) * 128 + m] = __float2half_rn(
                     tot[c] * __shfl_sync(0xffffffffu, asc_l[c >> 5], c & 31));
-            asm volatile("bar.sync 1, %0;" ::"n"(kFoldWarps * 32));
-            const int fw = warp - 8;
-            if (a.silu) {
-                const int n = mt * 64 + 2 * lane;  // two outputs per lane
-#pragma unroll 2
-                for (int c = fw; c < NT; c += kFoldWarps) {
-                    const int r = r0 + c;
-                    if (r >= P_valid) break;
-                    const __half2 gh = *reinterpret_cast<const __half2*>(&sm.otile[c * 128 + 2 * lane]);
-                    const __half2 uh = *reinterpret_cast<const __half2*>(&sm.otile[c * 128 + 64 + 2 * lane]);
-                    __half2 o;
-                    o.x = silu_mul_h(__low2half(gh), __low2half(uh));
-                    o.y = silu_mul_h(__high2half(gh), __high2half(uh));
-                    *reinterpret_cast<__half2*>(a.out16 + (int64_t)r * n_out + n) = o;
-                }
-            } else {
-                const int n = mt * 128 + 4 * lane;  // four outputs per lane
-                if (n < n_out)
-#pragma unroll 2
-                    for (int c = fw; c < NT; c += kFoldWarps) {
-                        const int r = r0 + c;
-                        if (r >= P_valid) break;
-                        *reinterpret_cast<uint2*>(a.out16 + (int64_t)r * n_out + n) =
-                            *reinterpret_cast<const uint2*>(&sm.otile[c * 128 + 4 * lane]);
-                    }
-            }
-            asm volatile("bar.sync 1, %0;" ::"n"(kFoldWarps * 32));
+            asm volatile("bar.sync 1, %0;" ::"n"(kFoldWarps * 32) : "memory");
+            pend_buf = buf;
+            pend_r0 = r0;
+            pend_mt = mt;
+            ++tiles_done;
+#if !W4A8_TC_DEFER
+            drain(0, NT);
+            pend_buf = -1;
+#endif
         }
+        if (pend_buf >= 0) drain(0, NT);
     }
 
     asm volatile("tcgen05.fence::before_thread_sync;" ::);

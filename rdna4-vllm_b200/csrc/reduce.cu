@@ -5,6 +5,8 @@
 //   out[t, n] = sum_{j ascending} w[t*top_k + j] * out2[slot_to_row[t*top_k + j], n]   (fp32)
 // The sum is a plain fp32 multiply then add in slot order, the order the reference oracle uses
 // (w4a8_fp8_wmma/test_moe_experts.py:182-190).
+#include <algorithm>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -97,4 +99,36 @@ extern "C" int w4a8_moe_gather_reduce(const void* out2, const int32_t* sorted_to
     }
     return launch_gather_reduce(static_cast<const __half*>(out2), map, topk_weights, out, false, M,
                                 N, (int)top_k, st);
+}
+
+namespace w4a8 {
+namespace {
+
+// out[r][i] = fp16(silu(fp16 gate)) * fp16 up with gate = x[r][i], up = x[r][I + i]: vLLM's
+// silu_and_mul on fp16 tensors, the step between gate_up and down in the unfused composition.
+__global__ void __launch_bounds__(256) silu_and_mul_kernel(const __half* __restrict__ x,
+                                                           __half* __restrict__ out, int64_t M,
+                                                           int64_t I) {
+    const int64_t n = M * I;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / I, c = i - r * I;
+        out[i] = silu_mul_h(x[r * 2 * I + c], x[r * 2 * I + I + c]);
+    }
+}
+
+}  // namespace
+}  // namespace w4a8
+
+extern "C" int w4a8_silu_and_mul(const void* x, void* out, int64_t M, int64_t inter,
+                                 w4a8_stream_t stream) {
+    using namespace w4a8;
+    if (M < 0 || inter < 0) return set_error("silu_and_mul: negative size");
+    if (M == 0 || inter == 0) return W4A8_OK;
+    if (!x || !out) return set_error("silu_and_mul: null pointer");
+    const int64_t n = M * inter;
+    const unsigned grid = (unsigned)std::min<int64_t>((n + 255) / 256, 148 * 16);
+    silu_and_mul_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        static_cast<const __half*>(x), static_cast<__half*>(out), M, inter);
+    return launch_status();
 }

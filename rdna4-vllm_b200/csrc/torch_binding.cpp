@@ -295,6 +295,18 @@ std::vector<at::Tensor> moe_align_block_size_forward(const at::Tensor& topk_ids,
     return {sorted, eids, ntp};
 }
 
+at::Tensor silu_and_mul_forward(const at::Tensor& x) {
+    TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kHalf && x.dim() == 2 && x.is_contiguous() &&
+                    x.size(1) % 2 == 0,
+                "x must be a contiguous (M, 2*inter) fp16 CUDA tensor");
+    const c10::cuda::CUDAGuard guard(x.device());
+    auto out = at::empty({x.size(0), x.size(1) / 2}, x.options());
+    check_status(w4a8_silu_and_mul(x.data_ptr(), out.data_ptr(), x.size(0), x.size(1) / 2,
+                                   cur_stream()),
+                 "silu_and_mul");
+    return out;
+}
+
 at::Tensor moe_decode_forward(const at::Tensor& x, const at::Tensor& w13, const at::Tensor& s13,
                               const at::Tensor& z13, const at::Tensor& w2, const at::Tensor& s2,
                               const at::Tensor& z2, const at::Tensor& topk_weights,
@@ -381,6 +393,7 @@ TORCH_LIBRARY_IMPL(w4a8_fp8_wmma, CUDA, m) {
 
 TORCH_LIBRARY(w4a8_b200, m) {
     m.def("act_quant_fp8(Tensor x) -> Tensor[]");
+    m.def("silu_and_mul(Tensor x) -> Tensor");
     // Whole gated MoE layer at decode sizes (align -> gate_up+SiLU -> down -> reduce).
     m.def("moe_decode(Tensor x, Tensor w13, Tensor s13, Tensor z13, Tensor w2, Tensor s2, "
           "Tensor z2, Tensor topk_weights, Tensor topk_ids) -> Tensor");
@@ -394,6 +407,7 @@ TORCH_LIBRARY(w4a8_b200, m) {
 
 TORCH_LIBRARY_IMPL(w4a8_b200, CUDA, m) {
     m.impl("act_quant_fp8", &act_quant_fp8_forward);
+    m.impl("silu_and_mul", &silu_and_mul_forward);
     m.impl("moe_decode", &moe_decode_forward);
     m.impl("moe_gemm1_silu", &gemm1_silu_impl);
     m.impl("moe_align_block_size", &moe_align_block_size_forward);

@@ -159,6 +159,12 @@ def moe_align_block_size(topk_ids: torch.Tensor, block_m: int, num_experts: int,
     return s, e, n
 
 
+def silu_and_mul(x: torch.Tensor) -> torch.Tensor:
+    """(M, 2*inter) fp16 [gate | up] -> (M, inter): fp16(g / (1 + exp(-g))) * up, the unfused
+    activation step between gate_up and down (the fused gate_up op applies the same epilogue)."""
+    return torch.ops.w4a8_b200.silu_and_mul(x.contiguous())
+
+
 # ---- Fake / meta impls (output contracts of the CUDA impls, reference __init__.py:240-297) ----
 _register_fake = getattr(getattr(torch, "library", None), "register_fake", None)
 if _register_fake is not None:
@@ -196,6 +202,10 @@ if _register_fake is not None:
                                        expert_ids, num_tokens_post_padded, topk_weights, output,
                                        top_k, block_m, kernel, weight_is_e2m1=False):
         return None
+
+    @_register_fake("w4a8_b200::silu_and_mul")
+    def _fake_silu_and_mul(x):
+        return x.new_empty((x.shape[0], x.shape[1] // 2), dtype=torch.float16)
 
     @_register_fake("w4a8_fp8_wmma::mmq_fp8_moe_gather_reduce")
     def _fake_mmq_fp8_moe_gather_reduce(out2, sorted_token_ids, topk_weights,

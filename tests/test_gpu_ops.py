@@ -354,3 +354,18 @@ def test_expert_parallel_layer_world1_vs_oracle(w4):
     w_full = np.concatenate([w, np.ones((T, 1), np.float32)], axis=1)
     ref = O.moe_layer(c["x"], p13, c["s13"], z13, p2, c["s2"], z2, ids_full, w_full)
     assert max_abs_rel(y, ref) <= MAX_ABS_REL
+
+
+def test_silu_and_mul_exhaustive_fp16_gate(w4):
+    """Every finite fp16 gate value (with a fixed up value of 1) through the library's SiLU
+    matches fp16(g / (1 + exp(-g))) computed by torch in fp32 with an IEEE divide, bit for bit:
+    the fused epilogue's fast quotient falls back to the exact divide at fp16 rounding
+    boundaries."""
+    bits = torch.arange(0, 65536, dtype=torch.int32).to(torch.int16).view(torch.float16)
+    g = bits[torch.isfinite(bits)].cuda()
+    for up in (1.0, -0.75):
+        x = torch.stack([g, torch.full_like(g, up)], 1).contiguous()  # (M, 2): inter = 1
+        out = w4.silu_and_mul(x)[:, 0]
+        gf = g.float()
+        ref = (gf / (1.0 + torch.exp(-gf))).to(torch.float16) * torch.tensor(up, dtype=torch.float16, device="cuda")
+        assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
