@@ -288,9 +288,10 @@ def _max_over_ranks(torch, dist, world, dev, v):
 
 def launches_per_step(workload: str, world: int) -> int:
     """Kernels of this library per step: decode = align count + place, operand quant, gate_up
-    GEMV + finish, down GEMV, gather-reduce (7); prefill adds the tile-path act-quant launches.
+    GEMV + finish, down GEMV, gather-reduce (7); prefill = align count + place, then per GEMM
+    operand quant + sorted-row gather + w4_tc_kernel (2 x 3), inverse map + gather-reduce (10).
     EP adds the shared expert's 7 and the combine gather-reduce."""
-    n = 7 if workload == "decode" else 9
+    n = 7 if workload == "decode" else 10
     if world > 1:
         n += 8
     return n
@@ -312,10 +313,15 @@ def _event_time(torch, fn, reps=20):
 
 def dominant_kernel(torch, args, world, dist, dev, x, ids, w13, s13, z13, E_total, T, recorded,
                     layer):
-    """The gate_up grouped GEMV op (operand quant + streaming GEMV + SiLU finish) on this
-    rank's rows, timed alone with CUDA events; algorithmic bytes = touched experts' w13 bytes
-    (codes + scales + zeros) + the fp16 activations read + the fp16 SiLU rows written."""
-    hbm, _, src = peaks()
+    """The gate_up op on this rank's rows, timed alone with CUDA events on the launching stream.
+
+    decode: the grouped GEMV op (operand quant + w4_stream_kernel + SiLU finish), HBM-bound;
+    algorithmic bytes = touched experts' w13 bytes (codes + scales + zeros) + the fp16
+    activations read + the fp16 SiLU rows written.
+    prefill: the tcgen05 tile op (operand quant + sorted-row gather + w4_tc_kernel with the
+    fused SiLU epilogue), tensor-bound; algorithmic FLOPs = 2 * routed rows * 2*inter * hidden
+    (padding rows not counted); peak = the dense e4m3 rate, twice the measured bf16 GEMM rate."""
+    hbm, fp8_peak, src = peaks()
     import w4a8_fp8_wmma as w4
     if world > 1:
         xr = recorded["rows"]
@@ -324,8 +330,8 @@ def dominant_kernel(torch, args, world, dist, dev, x, ids, w13, s13, z13, E_tota
         E_use, xx, ii = w13.size(0), xr, idr
     else:
         E_use, xx, ii = E_total, x, ids
-    block_m = 8 if xx.size(0) <= 96 or world > 1 else 64
-    kern = 7 if block_m == 8 else 6
+    prefill = args.workload == "prefill" and world == 1
+    block_m, kern = (128, 6) if prefill else (8, 7)
     s, e, n = w4.moe_align_block_size(ii, block_m, E_use)
 
     def launch():
@@ -335,6 +341,17 @@ def dominant_kernel(torch, args, world, dist, dev, x, ids, w13, s13, z13, E_tota
     valid = ii[(ii >= 0) & (ii < E_use)]
     touched = int(torch.unique(valid).numel())
     rows = int(valid.numel())
+    if prefill:
+        flops = 2.0 * rows * 2 * INTER * H
+        ach = flops / (ms / 1e3) / 1e12
+        return {"kernel": "gate_up tile op: operand_quant + tc_gather + w4_tc_kernel (SiLU epilogue)",
+                "bound": "tensor", "achieved": round(ach, 1), "peak": round(fp8_peak, 1),
+                "unit": "TFLOP/s", "frac": round(ach / fp8_peak, 4),
+                "peak_source": f"{src} (e4m3 dense = 2 x measured bf16)",
+                "algorithmic_flops_per_launch": flops, "avg_launch_us": round(ms * 1e3, 2),
+                "traffic": TC_KERNEL_TRAFFIC,
+                "traffic_source": "profiles/w4_tc_kernel_prefill.md (dram read+write of the "
+                                  "w4_tc_kernel launch, one ncu capture)"}
     bytes_ = touched * W13_BYTES + rows * H * 2 + rows * INTER * 2
     ach = bytes_ / (ms / 1e3) / 1e9
     return {"kernel": "gate_up grouped GEMV op: operand_quant + w4_stream_kernel + finish(SiLU)",
@@ -349,6 +366,9 @@ def dominant_kernel(torch, args, world, dist, dev, x, ids, w13, s13, z13, E_tota
 # dram__bytes_read.sum + dram__bytes_write.sum of the gate_up w4_stream_kernel launch in the
 # committed ncu capture (profiles/w4_stream_kernel_decode.md).
 STREAM_KERNEL_TRAFFIC = 185_420_544 + 4_915_968
+# The same for the prefill gate_up w4_tc_kernel launch (profiles/w4_tc_kernel_prefill.md);
+# None until that capture exists.
+TC_KERNEL_TRAFFIC = None
 
 
 def end_to_end(torch, dist, args, world, dev, x_np, ids_np, w_np, layer, run_grouped_moe,

@@ -147,16 +147,12 @@ extern "C" int w4a8_mmq_fp8_gemm(const void* x, const int32_t* w_packed, const v
         return launch_w4_stream(sa, st);
     }
     if (kernel != W4A8_DENSE_REFERENCE_SCALAR && kernel != W4A8_DENSE_DECODE_GEMV && M > 32 &&
-        tc_path_ok(K, (int)group_size, weight_is_e2m1, w_packed, 1 << 20)) {
-        if (int rc = launch_operand_quant(x, OperandOut{s.xq, s.scales, nullptr, s.xsum}, M, K,
-                                          nullptr, st))
-            return rc;
+        tc_path_ok(K, (int)group_size, weight_is_e2m1, w_packed, 1 << 20) &&
+        (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
         cudaError_t ce = cudaMemsetAsync(s.counter, 0, sizeof(int), st);
         if (ce != cudaSuccess) return (int)ce;
         TcArgs t{};
-        t.xq = s.xq;
-        t.act_scales = s.scales;
-        t.xsum = s.xsum;
+        t.x = static_cast<const __half*>(x);
         t.w = w_packed;
         t.scales = static_cast<const __half*>(scales);
         t.zeros = w_zeros;
@@ -282,16 +278,12 @@ int moe_launch(const char* op, int epi, const void* x, const int32_t* w_packed,
     }
     if (kernel == W4A8_MOE_WMMA && epi != kEpiScatter &&
         tc_path_ok(K, (int)group_size, e2m1, w_packed, (int)block_m) &&
+        (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
         (epi != kEpiSilu || (N / 2) % 64 == 0)) {
-        if (int rc = launch_operand_quant(x, OperandOut{s.xq, s.scales, nullptr, s.xsum}, x_rows,
-                                          K, nullptr, st))
-            return rc;
         cudaError_t ce = cudaMemsetAsync(s.counter, 0, sizeof(int), st);
         if (ce != cudaSuccess) return (int)ce;
         TcArgs t{};
-        t.xq = s.xq;
-        t.act_scales = s.scales;
-        t.xsum = s.xsum;
+        t.x = static_cast<const __half*>(x);
         t.w = w_packed;
         t.scales = static_cast<const __half*>(scales);
         t.zeros = w_zeros;

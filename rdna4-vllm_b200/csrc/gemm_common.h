@@ -90,9 +90,7 @@ int launch_w4_stream(StreamArgs a, cudaStream_t stream);
 // ---- tcgen05 tile GEMM (gemm_tc.cu) ----
 // Rows as in GemmArgs; activations are the operand quantiser's e4m3 bytes plus group sums.
 struct TcArgs {
-    const uint8_t* xq;          // (rows, K) e4m3, one row per source token
-    const float* act_scales;    // (rows,)
-    const float2* xsum;         // (rows, K/128) {K0, S}; S = sum of the group's activations
+    const __half* x;            // (x_rows, K) fp16 source rows (tokens, or the SiLU rows)
     uint8_t* xs;                // scratch (P_pad, K): sorted-order e4m3 rows (tc_carve)
     float* asc_s;               // scratch (P_pad,): sorted-order activation scales
     float* ssum;                // scratch (K/128, P_pad): sorted-order group sums, group-major

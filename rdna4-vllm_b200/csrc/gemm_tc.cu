@@ -1,9 +1,10 @@
 // gemm_tc.cu — W4A8 (grouped) GEMM tile path on the 5th-generation tensor cores (tcgen05).
 //
 // Two launches:
-//   1. tc_gather_kernel — copies each sorted row's e4m3 activation row, its activation scale and
-//      its per-group sums S into dense sorted-order buffers (padding rows become zeros), so the
-//      GEMM reads its token tiles with plain 2D TMA boxes instead of per-row gathers.
+//   1. tc_quant_rows_kernel — quantises each sorted row's source activations to e4m3 (per-token
+//      scale) and writes them, the scale and the per-group sums S into dense sorted-order
+//      buffers (padding rows become zeros), so the GEMM reads its token tiles with plain 2D
+//      TMA boxes instead of per-row gathers.
 //   2. w4_tc_kernel — persistent and warp-specialised, one CTA per SM. A tile is 128 weight
 //      rows x NT sorted rows (NT = 64 or 128; a tile never straddles an expert block). Tiles are
 //      dealt round-robin to the CTAs; inside a CTA every role walks the same tile sequence and
@@ -678,9 +679,13 @@ w4_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmw,
     }
 }
 
-// One warp per sorted row: dense sorted-order operand rows for the tile kernel. Rows past the
-// last valid one (up to the tile-rounded count) and rows with a sentinel id are zero-filled.
-__global__ void __launch_bounds__(256) tc_gather_kernel(const TcArgs a, int NT) {
+// One warp per sorted row: the row's source activations are quantised per token to e4m3
+// exactly as act_quant_fp8 does (a_scale = max(amax, 4.48e-6) / 448, q = e4m3_rn(x / a_scale),
+// IEEE divides; w4a8_fp8_wmma/test_correctness.py:74-76) and written in sorted order together
+// with the scale and the per-group sums S of the e4m3 values, so the tile kernel reads its token
+// tiles with plain 2D TMA boxes. Rows past the last valid one (up to the tile-rounded count)
+// and rows with a sentinel id are zero-filled. Requires K % 256 == 0.
+__global__ void __launch_bounds__(256) tc_quant_rows_kernel(const TcArgs a, int NT) {
     const int lane = threadIdx.x & 31;
     const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
     const int P_valid = a.ntp ? min(a.ntp[0], a.P) : a.P;
@@ -693,18 +698,53 @@ __global__ void __launch_bounds__(256) tc_gather_kernel(const TcArgs a, int NT) 
         if (e >= 0 && e < a.E && sid >= 0 && sid < a.num_valid)
             src = a.src_identity ? (int)r : sid / a.top_k;
     }
-    uint4* dst = reinterpret_cast<uint4*>(a.xs + r * a.K);
-    const int64_t nv = a.K / 16;
-    if (src >= 0) {
-        const uint4* sp = reinterpret_cast<const uint4*>(a.xq + (int64_t)src * a.K);
-        for (int64_t i = lane; i < nv; i += 32) dst[i] = __ldg(sp + i);
-        for (int g = lane; g < a.G; g += 32)
-            a.ssum[(int64_t)g * a.P_pad + r] = a.xsum[(int64_t)src * a.G + g].y;
-        if (lane == 0) a.asc_s[r] = a.act_scales[src];
-    } else {
-        for (int64_t i = lane; i < nv; i += 32) dst[i] = make_uint4(0, 0, 0, 0);
+    uint2* dst = reinterpret_cast<uint2*>(a.xs + r * a.K);
+    const int nch = (int)(a.K / 8);  // 8-element chunks; chunk i belongs to group i / 16
+    if (src < 0) {
+        for (int i = lane; i < nch; i += 32) dst[i] = make_uint2(0u, 0u);
         for (int g = lane; g < a.G; g += 32) a.ssum[(int64_t)g * a.P_pad + r] = 0.f;
         if (lane == 0) a.asc_s[r] = 0.f;
+        return;
+    }
+    const uint4* xr = reinterpret_cast<const uint4*>(a.x + (int64_t)src * a.K);
+    float amax = 0.f;
+    for (int i = lane; i < nch; i += 32) {
+        const uint4 v = __ldg(xr + i);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const __half2 h = __habs2(*reinterpret_cast<const __half2*>(&w[j]));
+            amax = fmaxf(amax, fmaxf(__low2float(h), __high2float(h)));
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float s = __fdiv_rn(fmaxf(amax, kAmaxFloor), kE4m3Max);
+    if (lane == 0) a.asc_s[r] = s;
+    for (int i0 = 0; i0 < nch; i0 += 32) {  // nch % 32 == 0: lanes 0-15 / 16-31 = one group each
+        const int i = i0 + lane;
+        const uint4 v = __ldg(xr + i);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint32_t q[2];
+        float sum = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; j += 2) {
+            const __half2 h0 = *reinterpret_cast<const __half2*>(&w[j]);
+            const __half2 h1 = *reinterpret_cast<const __half2*>(&w[j + 1]);
+            const uint16_t p0 = f32x2_to_e4m3x2(__fdiv_rn(__low2float(h0), s),
+                                                __fdiv_rn(__high2float(h0), s));
+            const uint16_t p1 = f32x2_to_e4m3x2(__fdiv_rn(__low2float(h1), s),
+                                                __fdiv_rn(__high2float(h1), s));
+            q[j / 2] = (uint32_t)p0 | ((uint32_t)p1 << 16);
+            const uint32_t e0 = e4m3x2_to_f16x2(p0), e1 = e4m3x2_to_f16x2(p1);
+            const float2 d0 = __half22float2(*reinterpret_cast<const __half2*>(&e0));
+            const float2 d1 = __half22float2(*reinterpret_cast<const __half2*>(&e1));
+            sum += (d0.x + d0.y) + (d1.x + d1.y);
+        }
+        dst[i] = make_uint2(q[0], q[1]);
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if ((lane & 15) == 0) a.ssum[(int64_t)(i / 16) * a.P_pad + r] = sum;
     }
 }
 
@@ -747,7 +787,7 @@ int sm_count() {
 template <int NT>
 int launch_tc_t(const TcArgs& a, cudaStream_t stream) {
     const int64_t rows_max = (int64_t)(a.P + NT - 1) / NT * NT;
-    tc_gather_kernel<<<(unsigned)((rows_max + 7) / 8), 256, 0, stream>>>(a, NT);
+    tc_quant_rows_kernel<<<(unsigned)((rows_max + 7) / 8), 256, 0, stream>>>(a, NT);
     if (int rc = launch_status()) return rc;
     CUtensorMap tmw, tmx;
     if (!make_map(&tmw, a.w, (uint64_t)a.E * a.N, (uint64_t)a.K / 2, 64, a.silu ? 64 : 128,
@@ -771,7 +811,7 @@ int launch_tc_t(const TcArgs& a, cudaStream_t stream) {
 }  // namespace
 
 bool tc_path_ok(int64_t K, int group_size, int e2m1, const void* w, int block_m) {
-    return !e2m1 && group_size == 128 && K % 128 == 0 && K >= 128 &&
+    return !e2m1 && group_size == 128 && K % 256 == 0 && K >= 256 &&
            (reinterpret_cast<uintptr_t>(w) & 15) == 0 && block_m % 64 == 0;
 }
 
