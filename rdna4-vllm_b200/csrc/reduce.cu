@@ -23,7 +23,8 @@ __global__ void build_inverse_map_kernel(const int32_t* __restrict__ sorted_ids,
     if (slot >= 0 && slot < num_slots) slot_to_row[slot] = (int32_t)r;
 }
 
-// One CTA per (token, 512-channel chunk); each thread reduces 2 adjacent channels.
+// One CTA per (token, 512-channel chunk); each thread reduces 2 adjacent channels. Generic
+// path for N % 8 != 0 or unaligned rows.
 template <typename OutT>
 __global__ void __launch_bounds__(256)
 gather_reduce_kernel(const __half* __restrict__ out2, const int32_t* __restrict__ slot_to_row,
@@ -52,20 +53,82 @@ gather_reduce_kernel(const __half* __restrict__ out2, const int32_t* __restrict_
     if (pair) out[t * N + n + 1] = (OutT)a1;
 }
 
+// Vector path (N % 8 == 0, 16-byte aligned rows): one warp-row of 8-channel chunks per thread;
+// the top_k row indices and weights of the token are staged once per CTA, then every slot's
+// 16-byte row chunk is requested before the in-order accumulation.
+constexpr int kMaxTopK = 16;
+template <typename OutT>
+__global__ void __launch_bounds__(256)
+gather_reduce_vec_kernel(const __half* __restrict__ out2, const int32_t* __restrict__ slot_to_row,
+                         const float* __restrict__ topk_w, OutT* __restrict__ out, int64_t N,
+                         int top_k) {
+    __shared__ int32_t rows[kMaxTopK];
+    __shared__ float wts[kMaxTopK];
+    const int64_t t = blockIdx.y;
+    if (threadIdx.x < top_k) {
+        rows[threadIdx.x] = slot_to_row[t * top_k + threadIdx.x];
+        wts[threadIdx.x] = topk_w[t * top_k + threadIdx.x];
+    }
+    __syncthreads();
+    const int64_t n = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+    if (n >= N) return;
+    uint4 v[kMaxTopK];
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j)
+        if (j < top_k && rows[j] >= 0)
+            v[j] = __ldg(reinterpret_cast<const uint4*>(out2 + (int64_t)rows[j] * N + n));
+    float acc[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[c] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j) {
+        if (j < top_k && rows[j] >= 0) {
+            const float w = wts[j];
+            const uint32_t h[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h[c]));
+                acc[2 * c] = __fadd_rn(acc[2 * c], __fmul_rn(w, f.x));
+                acc[2 * c + 1] = __fadd_rn(acc[2 * c + 1], __fmul_rn(w, f.y));
+            }
+        }
+    }
+    if constexpr (sizeof(OutT) == 4) {
+        float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + t * N + n);
+        o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    } else {
+        uint4 o;
+        uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const __half2 h2 = __floats2half2_rn(acc[2 * c], acc[2 * c + 1]);
+            ow[c] = *reinterpret_cast<const uint32_t*>(&h2);
+        }
+        *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(out) + t * N + n) = o;
+    }
+}
+
 }  // namespace
 
 int launch_gather_reduce(const __half* out2, const int32_t* slot_to_row, const float* topk_w,
                          void* out, bool out_half, int64_t M, int64_t N, int top_k,
                          cudaStream_t stream) {
     if (M <= 0) return W4A8_OK;
-    const dim3 grid((unsigned)((N + 511) / 512), (unsigned)M);
-    if (out_half)
-        gather_reduce_kernel<__half><<<grid, 256, 0, stream>>>(out2, slot_to_row, topk_w,
-                                                               static_cast<__half*>(out), N, top_k);
-    else
-        gather_reduce_kernel<float><<<grid, 256, 0, stream>>>(out2, slot_to_row, topk_w,
-                                                              static_cast<float*>(out), N, top_k);
-    return launch_status();
+    const bool vec = N % 8 == 0 && top_k <= kMaxTopK &&
+                     (reinterpret_cast<uintptr_t>(out2) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+    if (vec) {
+        const dim3 grid((unsigned)((N / 8 + 255) / 256), (unsigned)M);
+        if (out_half)
+            gather_reduce_vec_kernel<__half><<<grid, 256, 0, stream>>>(
+                out2, slot_to_row, topk_w, static_cast<__half*>(out), N, top_k);
+        else
+            gather_reduce_vec_kernel<float><<<grid, 256, 0, stream>>>(
+                out2, slot_to_row, topk_w, static_cast<float*>(out), N, top_k);
+        return launch_status();
+    }
+    const dim3 grid((unsigned)((N + 511) / 512), (unsigned)M);    return launch_status();
 }
 
 }  // namespace w4a8
