@@ -80,9 +80,11 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
 }
 
 // mma.sync m16n8k16, f16 x f16 -> f32 (D = A*B + C).
+// Not volatile: a pure function of its operands, so the compiler may interleave independent
+// MMAs (their latency on sm_100 is long).
 __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                           uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
         "{%8,%9}, {%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])

@@ -44,6 +44,7 @@
 #include "common.cuh"
 #include "gemm_common.h"
 #include "internal.h"
+#include "sm100.cuh"
 
 namespace w4a8 {
 
@@ -53,7 +54,6 @@ namespace {
 #define W4A8_TC_DEFER 0
 #endif
 constexpr int kTcThreads = 512;
-constexpr uint64_t kWaitLimitNs = 1000000000ull;   // a wait gives up after 1 s
 constexpr int kFoldWarps = 8;
 
 template <int NT>
@@ -92,10 +92,6 @@ struct TcSmem {
 static_assert(sizeof(TcSmem<128>) + 1024 <= 227 * 1024, "tile kernel shared memory");
 static_assert(sizeof(TcSmem<64>) + 1024 <= 227 * 1024, "tile kernel shared memory");
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
-
 // UMMA shared-memory descriptor, K-major with the 128-byte swizzle: 8-row atoms of 128 bytes,
 // atoms 1024 bytes apart (SBO); the leading offset is unused for swizzled K-major operands.
 __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
@@ -110,74 +106,6 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
 // kind::f8f6f4 instruction descriptor: fp32 accumulate, A = B = e4m3, both K-major.
 __host__ __device__ constexpr uint32_t umma_idesc(int M, int N) {
     return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-                 "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return done != 0;
-}
-__device__ __forceinline__ uint64_t global_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-// Bounded wait: try_wait in a loop (the instruction itself suspends the thread for a short,
-// hardware-defined time), giving up after kWaitLimitNs; once any wait in the CTA has given up,
-// later waits return at once.
-__device__ __forceinline__ void mbar_wait(uint64_t* bar, uint32_t parity, volatile int* bad) {
-    if (mbar_try(bar, parity)) return;
-    if (*bad) return;
-    const uint64_t t0 = global_ns();
-    for (uint32_t i = 1;; ++i) {
-        if (mbar_try(bar, parity)) return;
-        if ((i & 255) == 0) {
-            if (*bad) return;
-            if (global_ns() - t0 > kWaitLimitNs) {
-                *bad = 1;
-                return;
-            }
-        }
-    }
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
-                                            uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
-    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                     reinterpret_cast<uint64_t>(map)),
-                 "r"(x), "r"(y)
-                 : "memory");
-}
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
-                                          uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-        ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
 }
 
 // 8 codes (nibble i of `w` = code i) -> 8 e4m3 bytes of the codes' values, codes 0..3 in `lo`
@@ -288,8 +216,10 @@ w4_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmw,
              const __grid_constant__ CUtensorMap tmx) {
     using C = TcCfg<NT>;
     extern __shared__ uint8_t smem_raw[];
+    // 1024-byte alignment by offsetting the __shared__ array itself (a round trip through an
+    // integer would lose the shared address space and turn every access into a generic one)
     TcSmem<NT>& sm = *reinterpret_cast<TcSmem<NT>*>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+        smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     volatile int* bad = &sm.bad;
 
@@ -809,6 +739,11 @@ int launch_tc_t(const TcArgs& a, cudaStream_t stream) {
 }
 
 }  // namespace
+
+bool make_tma_map_u8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t row_bytes,
+                     uint32_t box_bytes, uint32_t box_rows, CUtensorMapSwizzle sw) {
+    return make_map(map, base, rows, row_bytes, box_bytes, box_rows, sw);
+}
 
 bool tc_path_ok(int64_t K, int group_size, int e2m1, const void* w, int block_m) {
     return !e2m1 && group_size == 128 && K % 256 == 0 && K >= 256 &&

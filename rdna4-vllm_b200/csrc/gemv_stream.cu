@@ -1,11 +1,14 @@
 // gemv_stream.cu — persistent W4A8 GEMV for decode-sized row counts.
 //
 // Work item = (8-row block b of the padded-sorted rows, K split ks of 4 groups, 128-row group
-// rg of the weight rows). CTAs (8 warps, 2 per SM) walk items round-robin; warp w computes the
-// 16 weight rows rg*128 + 16w .. +15 of an item. While item i is computed the CTA has already
-// issued item i+1's weight loads (register double buffer of 128-bit non-allocating loads) and
-// its activation tile, group scales, zero points and activation group sums (cp.async into the
-// other half of a shared double buffer); warp 0 meanwhile fetches item i+2's routing rows.
+// rg of the weight rows). One CTA per SM walks items round-robin. A producer warp streams each
+// item into a ring of shared-memory stages, so several items' weights are in flight per SM:
+//   - the 128 x 256-byte weight tile: two 2D TMA boxes with the 128-byte swizzle;
+//   - the 8 activation rows (fp16 operand, 1 KB each) and their group sums: bulk copies
+//     straight from the source rows (the gather happens in the copy);
+//   - scales and zero points: cp.async, completing on the same mbarrier.
+// Eight compute warps each take 16 weight rows of the item (mma.sync.m16n8k16, 8 token
+// columns) and release the stage.
 //
 // Arithmetic. Per 128-code group a lane expands 2 weight rows x 32 codes with the fp16
 // magic-number trick without subtracting the zero point: pairs (0,4),(2,6) of every 8-code word
@@ -22,39 +25,49 @@
 //
 // K splits write fp32 partials [ks][row][n]; w4_stream_finish_kernel sums them in fixed order
 // (results do not depend on scheduling) and applies the epilogue. One split: direct epilogue.
+// Every mbarrier wait is bounded (sm100.cuh); once one gives up, later waits are skipped, the
+// kernel finishes and sets bit 1 of StreamArgs::counter.
 #include <algorithm>
 
 #include "common.cuh"
 #include "gemm_common.h"
 #include "internal.h"
+#include "sm100.cuh"
 
 namespace w4a8 {
 
 namespace {
 
-constexpr int kWarps = 8;
+constexpr int kWarps = 8;                        // compute warps
+constexpr int kStreamThreads = (kWarps + 1) * 32;
 constexpr int kSpi = 4;                          // K blocks (groups of 128) per item
 constexpr int kRowsPerItem = kWarps * 16;        // 128 weight rows
 constexpr int kActStride = kSpi * 256 + 32;      // bytes per activation row in shared memory
+constexpr int kStages = 5;
 
+// Shared position of operand chunk (k-block kb, lane column c, unit u) within an activation
+// row: the unit index is XOR-ed with bit 1 of c so that the 8 rows x 4 columns of one mma.sync
+// B fragment read hit distinct banks. The operand quantiser stores xh in this order, so a
+// linear copy of a row lands in place.
 __device__ __forceinline__ int act_off(int kb, int c, int u) {
     return kb * 256 + c * 64 + ((u ^ ((c >> 1) & 1)) << 4);
 }
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
-    const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
-    const int n = pred ? 16 : 0;
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(n));
+__device__ __forceinline__ void cp_async8_bar(void* smem, const void* gmem, bool pred) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(smem_u32(smem)), "l"(gmem),
+                 "r"(pred ? 8 : 0));
 }
-__device__ __forceinline__ void cp_async8(void* smem, const void* gmem, bool pred) {
-    const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
-    const int n = pred ? 8 : 0;
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(s), "l"(gmem), "r"(n));
+__device__ __forceinline__ void cp_async16_bar(void* smem, const void* gmem, bool pred) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem),
+                 "r"(pred ? 16 : 0));
 }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::); }
+// Arrive on `bar` once this thread's earlier cp.async copies have landed.
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
 
 struct ItemMeta {
-    int item;     // item index (>= total: none)
     int any;      // 1 when at least one of the 8 rows is live
     int e;        // expert
     int b, ks, rg;
@@ -62,12 +75,16 @@ struct ItemMeta {
     int sid[8];
 };
 
-struct Smem {
-    uint8_t act[2][8][kActStride];
-    float2 xs[2][kSpi][8];                   // {K0, S} per (group, token column)
-    __half sc[2][kRowsPerItem][kSpi];
-    uint32_t zr[2][kRowsPerItem / 8][kSpi];
-    ItemMeta meta[3];
+struct StreamSmem {
+    uint8_t wt[kStages][2][128 * 128];       // weight tile halves, SW128 (1024-aligned)
+    uint8_t act[kStages][8][kActStride];     // activation rows
+    float2 xs[kStages][8][kSpi];             // {K0, S} per (token column, group)
+    __half sc[kStages][kRowsPerItem][kSpi];
+    uint32_t zr[kStages][kRowsPerItem / 8][kSpi];
+    ItemMeta meta[kStages];
+    uint64_t full[kStages];
+    uint64_t empty[kStages];
+    int bad;
 };
 
 // 8 codes of one word -> 4 half2 (pairs (0,4),(1,5),(2,6),(3,7)): 1024+q and 1024+16q.
@@ -80,108 +97,95 @@ __device__ __forceinline__ void expand_word(uint32_t w, uint32_t (&h)[4]) {
     h[3] = and_or(w8, 0x00F000F0u, kMagic);
 }
 
-// Item metadata is produced by warp 0 in two halves so that its L2 latency hides under the
-// warp's own compute: meta_issue() loads the raw routing values into registers, and
-// meta_publish() (after the compute) derives the rows and writes the shared slot.
-struct MetaRegs {
-    int item, e, sid;
+// Routing values of one item, loaded one item ahead of their use by the producer.
+struct ItemRoute {
+    int sid, e;
 };
-
-__device__ __forceinline__ MetaRegs meta_issue(const StreamArgs& a, int item, int total,
-                                               int per_b, int P_valid) {
+__device__ __forceinline__ ItemRoute fetch_route(const StreamArgs& a, int item, int per_b,
+                                                 int P_valid, int total) {
     const int lane = threadIdx.x & 31;
-    MetaRegs r{item, -1, -1};
+    ItemRoute r{-1, -1};
     if (item < total) {
-        const int row = (item / per_b) * 8 + lane;
+        const int b = item / per_b;
+        const int row = b * 8 + lane;
         if (lane < 8 && row < P_valid) r.sid = a.sorted_ids ? a.sorted_ids[row] : row;
-        r.e = a.expert_ids ? a.expert_ids[((item / per_b) * 8) / a.block_m] : 0;
+        r.e = a.expert_ids ? a.expert_ids[(b * 8) / a.block_m] : 0;
     }
     return r;
 }
 
-__device__ __forceinline__ void meta_publish(const StreamArgs& a, const MetaRegs& r, int total,
-                                             int per_b, ItemMeta& m) {
+// Producer (whole warp): item metadata, then the item's copies into stage `st`.
+__device__ __forceinline__ void produce_item(const StreamArgs& a, StreamSmem& sm,
+                                             const CUtensorMap* tmw, int item, int per_b,
+                                             int P_valid, int st, const ItemRoute& rt) {
     const int lane = threadIdx.x & 31;
-    const bool live = r.item < total && r.e >= 0 && r.e < a.E;
-    const bool ok = live && lane < 8 && r.sid >= 0 && r.sid < a.num_valid;
+    const int b = item / per_b, rem = item - b * per_b;
+    const int ks = rem / a.rg_n, rg = rem - ks * a.rg_n;
+    const int row = b * 8 + lane;
+    const int sid = rt.sid;
+    const int e = rt.e;
+    const bool live = e >= 0 && e < a.E;
+    const bool ok = live && lane < 8 && sid >= 0 && sid < a.num_valid;
+    const int src = ok ? (a.src_identity ? row : sid / a.top_k) : -1;
     const int any = __any_sync(0xffffffffu, ok);
+    const uint32_t okm = __ballot_sync(0xffffffffu, ok);
+    ItemMeta& m = sm.meta[st];
     if (lane < 8) {
-        m.src[lane] = ok ? (a.src_identity ? (r.item / per_b) * 8 + lane : r.sid / a.top_k) : -1;
-        m.sid[lane] = ok ? r.sid : 0;
+        m.src[lane] = src;
+        m.sid[lane] = ok ? sid : 0;
     }
-    if (lane == 0) {
-        const int b = r.item / per_b, rem = r.item - b * per_b;
-        m.item = r.item;
-        m.any = any;
-        m.e = r.e;
-        m.b = b;
-        m.ks = rem / a.rg_n;
-        m.rg = rem - m.ks * a.rg_n;
-    }
-}
-
-// All threads: cp.async the activation tile, group sums, scales and zero points of a live
-// item into buffer `buf`.
-__device__ __forceinline__ void stage_item(const StreamArgs& a, Smem& sm, const ItemMeta& m,
-                                           int buf) {
-    const int tid = threadIdx.x;
-    const int64_t k0 = (int64_t)m.ks * kSpi * 128;
-    const int kb0 = m.ks * kSpi;
-    for (int idx = tid; idx < 8 * 64; idx += blockDim.x) {  // 8 rows x 512 fp16
-        const int row = idx >> 6, q = idx & 63;
-        const int src = m.src[row];
-        const __half* g = a.xh + (int64_t)max(src, 0) * a.K + k0 + q * 8;
-        cp_async16(&sm.act[buf][row][act_off(q >> 4, (q >> 2) & 3, q & 3)], g, src >= 0);
-    }
-    const int n0 = m.rg * kRowsPerItem;
-    if (tid < kRowsPerItem) {  // scales: 128 rows x 4 groups
-        const int n = n0 + tid;
-        const bool ok = n < a.N;
-        const __half* g = a.scales + ((int64_t)m.e * a.N + (ok ? n : 0)) * a.G + kb0;
-        cp_async8(&sm.sc[buf][tid][0], g, ok);
-    } else if (tid < kRowsPerItem + kRowsPerItem / 8) {  // zero points: 16 words x 4 groups
-        const int j = tid - kRowsPerItem;
-        const int n8 = n0 / 8 + j;
-        if (a.zeros && n8 < a.N / 8)
-            cp_async16(&sm.zr[buf][j][0], a.zeros + ((int64_t)m.e * (a.N / 8) + n8) * a.G + kb0,
-                       true);
-    } else if (tid < kRowsPerItem + kRowsPerItem / 8 + 32) {  // group sums: 4 groups x 8 rows
-        const int j = tid - kRowsPerItem - kRowsPerItem / 8;
-        const int grp = j >> 3, col = j & 7;
-        const int src = m.src[col];
-        const float2* g = a.xsum + (int64_t)max(src, 0) * a.G + kb0 + grp;
-        cp_async8(&sm.xs[buf][grp][col], g, src >= 0);
-    }
-    asm volatile("cp.async.commit_group;" ::);
-}
-
-struct WeightRegs {
-    uint4 w[kSpi][2];
-};
-
-__device__ __forceinline__ void load_weights(const StreamArgs& a, const ItemMeta& m, int warp,
-                                             int lane, WeightRegs& r) {
-    const int64_t kw = a.K / 8;
-    const int n0 = m.rg * kRowsPerItem + warp * 16 + (lane >> 2);
-    const int row0 = min(n0, a.N - 1), row1 = min(n0 + 8, a.N - 1);
-    const int32_t* base = a.w + (int64_t)m.e * a.N * kw + (m.ks * kSpi) * 16 + (lane & 3) * 4;
+    if (any) {
+        const int kb0 = ks * kSpi;
+        const int n0 = rg * kRowsPerItem;
 #pragma unroll
-    for (int j = 0; j < kSpi; ++j) {
-        if (m.ks * kSpi + j < a.G) {
-            r.w[j][0] = ldg_stream(base + (int64_t)row0 * kw + j * 16);
-            r.w[j][1] = ldg_stream(base + (int64_t)row1 * kw + j * 16);
-        } else {
-            r.w[j][0] = r.w[j][1] = make_uint4(0, 0, 0, 0);
+        for (int i = 0; i < kRowsPerItem / 32; ++i) {  // scales: 128 rows x 4 groups (8 B)
+            const int r = lane + 32 * i, n = n0 + r;
+            const bool nok = n < a.N;
+            cp_async8_bar(&sm.sc[st][r][0], a.scales + ((int64_t)e * a.N + (nok ? n : 0)) * a.G + kb0,
+                          nok);
+        }
+        if (lane < kRowsPerItem / 8) {  // zero points: 16 words x 4 groups
+            const int n8 = n0 / 8 + lane;
+            const bool zok = a.zeros && n8 < a.N / 8;
+            cp_async16_bar(&sm.zr[st][lane][0],
+                           zok ? (const void*)(a.zeros + ((int64_t)e * (a.N / 8) + n8) * a.G + kb0)
+                               : (const void*)a.scales,
+                           zok);
         }
     }
+    __syncwarp();
+    if (lane == 0) {
+        m.any = any;
+        m.e = e;
+        m.b = b;
+        m.ks = ks;
+        m.rg = rg;
+        uint64_t* fb = &sm.full[st];
+        if (any) {
+            const uint32_t bytes = 2 * 128 * 128 + (uint32_t)__popc(okm) * (kSpi * 256 + kSpi * 8);
+            mbar_expect_tx(fb, bytes);
+            const int y = e * a.N + rg * kRowsPerItem;
+            tma_load_2d(&sm.wt[st][0][0], tmw, ks * 256, y, fb);
+            tma_load_2d(&sm.wt[st][1][0], tmw, ks * 256 + 128, y, fb);
+            for (int c = 0; c < 8; ++c) {
+                if (!(okm >> c & 1u)) continue;
+                const int srow = m.src[c];
+                bulk_load(&sm.act[st][c][0], a.xh + (int64_t)srow * a.K + (int64_t)ks * kSpi * 128,
+                          kSpi * 256, fb);
+                bulk_load(&sm.xs[st][c][0], a.xsum + (int64_t)srow * a.G + ks * kSpi, kSpi * 8, fb);
+            }
+        } else {
+            mbar_arrive(fb);
+        }
+    }
+    cp_async_arrive(&sm.full[st]);
 }
 
-// Compute one item from registers + shared buffer `buf`; emit partials or the epilogue.
-__device__ __forceinline__ void compute_item(const StreamArgs& a, const Smem& sm,
-                                             const ItemMeta& m, int buf, int warp, int lane,
-                                             const WeightRegs& r) {
+// Compute one item (this warp's 16 weight rows) from stage `st`; emit partials or the epilogue.
+__device__ __forceinline__ void compute_item(const StreamArgs& a, const StreamSmem& sm, int st,
+                                             int warp, int lane, int P_valid) {
+    const ItemMeta& m = sm.meta[st];
     const int c = lane & 3, tok = lane >> 2;
-    // item fields into registers once (the shared slot would be re-read after every MMA)
     const int m_any = m.any, m_b = m.b, m_ks = m.ks, m_rg = m.rg;
     const int nl = warp * 16 + tok;              // local row (0..127) of the item
     const int n0 = m_rg * kRowsPerItem + nl;
@@ -190,7 +194,6 @@ __device__ __forceinline__ void compute_item(const StreamArgs& a, const Smem& sm
     if (!m_any) {
         // all-padding block or non-local expert: rows are zeros for the direct store epilogue
         if (a.mode == kStreamStore && !a.force_part) {
-            const int P_valid = a.ntp ? min(a.ntp[0], a.P) : a.P;
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) {
                 const int rr = m_b * 8 + 2 * c + (jj & 1), n = n0 + (jj >> 1) * 8;
@@ -201,14 +204,18 @@ __device__ __forceinline__ void compute_item(const StreamArgs& a, const Smem& sm
     }
     const int src_c[2] = {m.src[2 * c], m.src[2 * c + 1]};
     const int sid_c[2] = {m.sid[2 * c], m.sid[2 * c + 1]};
-    const uint8_t* rowp = &sm.act[buf][tok][0];
+    const uint8_t* rowp = &sm.act[st][tok][0];
     const int sh0 = (n0 & 7) * 4, sh1 = ((n0 + 8) & 7) * 4;
-    const int nj = min(kSpi, a.G - m_ks * kSpi);
+    const int r0 = nl, r1 = nl + 8;              // tile rows of this lane
 #pragma unroll
     for (int j = 0; j < kSpi; ++j) {
-        if (j >= nj) break;
-        const uint32_t w0[4] = {r.w[j][0].x, r.w[j][0].y, r.w[j][0].z, r.w[j][0].w};
-        const uint32_t w1[4] = {r.w[j][1].x, r.w[j][1].y, r.w[j][1].z, r.w[j][1].w};
+        // weight chunk (16 B) c of group j: tile half j / 2, chunk (j % 2) * 4 + c, swizzled
+        const uint8_t* wh = &sm.wt[st][j >> 1][0];
+        const int u = (j & 1) * 4 + c;
+        const uint4 q0 = *reinterpret_cast<const uint4*>(wh + r0 * 128 + ((u ^ (r0 & 7)) << 4));
+        const uint4 q1 = *reinterpret_cast<const uint4*>(wh + r1 * 128 + ((u ^ (r1 & 7)) << 4));
+        const uint32_t w0[4] = {q0.x, q0.y, q0.z, q0.w};
+        const uint32_t w1[4] = {q1.x, q1.y, q1.z, q1.w};
         // two independent accumulator chains (words 0,2 and 1,3) halve the MMA dependency depth
         float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
@@ -222,20 +229,22 @@ __device__ __forceinline__ void compute_item(const StreamArgs& a, const Smem& sm
             const uint32_t a1[4] = {h0[2], h1[2], h0[3], h1[3]};
             mma_16816(acc[i & 1], a1, bq.z, bq.w);
         }
+#pragma unroll
+        for (int v = 0; v < 4; ++v) acc[0][v] += acc[1][v];
         float z0 = 8.f, z1 = 8.f;
         if (a.zeros) {
             // nibble -> float through the 2^23 magic (one LOP3 + one FADD, no conversion unit)
-            z0 = __uint_as_float(0x4B000000u | ((sm.zr[buf][nl >> 3][j] >> sh0) & 0xF)) - 8388608.f;
-            z1 = __uint_as_float(0x4B000000u | ((sm.zr[buf][(nl + 8) >> 3][j] >> sh1) & 0xF)) -
+            z0 = __uint_as_float(0x4B000000u | ((sm.zr[st][nl >> 3][j] >> sh0) & 0xF)) - 8388608.f;
+            z1 = __uint_as_float(0x4B000000u | ((sm.zr[st][(nl + 8) >> 3][j] >> sh1) & 0xF)) -
                  8388608.f;
         }
-        const float4 xs = *reinterpret_cast<const float4*>(&sm.xs[buf][j][2 * c]);  // K0,S x 2 cols
-        const float s0 = __half2float(sm.sc[buf][nl][j]);
-        const float s1 = __half2float(sm.sc[buf][nl + 8][j]);
-        tot[0] = fmaf(s0, fmaf(-z0, xs.y, (acc[0][0] + acc[1][0]) - xs.x), tot[0]);
-        tot[1] = fmaf(s0, fmaf(-z0, xs.w, (acc[0][1] + acc[1][1]) - xs.z), tot[1]);
-        tot[2] = fmaf(s1, fmaf(-z1, xs.y, (acc[0][2] + acc[1][2]) - xs.x), tot[2]);
-        tot[3] = fmaf(s1, fmaf(-z1, xs.w, (acc[0][3] + acc[1][3]) - xs.z), tot[3]);
+        const float2 xa = sm.xs[st][2 * c][j], xb = sm.xs[st][2 * c + 1][j];  // {K0, S}
+        const float s0 = __half2float(sm.sc[st][nl][j]);
+        const float s1 = __half2float(sm.sc[st][nl + 8][j]);
+        tot[0] = fmaf(s0, fmaf(-z0, xa.y, acc[0][0] - xa.x), tot[0]);
+        tot[1] = fmaf(s0, fmaf(-z0, xb.y, acc[0][1] - xb.x), tot[1]);
+        tot[2] = fmaf(s1, fmaf(-z1, xa.y, acc[0][2] - xa.x), tot[2]);
+        tot[3] = fmaf(s1, fmaf(-z1, xb.y, acc[0][3] - xb.x), tot[3]);
     }
     // tot[0..1]: row n0, token columns 2c, 2c+1; tot[2..3]: row n0 + 8.
 #pragma unroll
@@ -254,7 +263,6 @@ __device__ __forceinline__ void compute_item(const StreamArgs& a, const Smem& sm
                           a.topk_weights[sid] * tot[jj] * a.act_scales[src]);
             }
         } else {  // store
-            const int P_valid = a.ntp ? min(a.ntp[0], a.P) : a.P;
             if (rr < P_valid)
                 a.out16[(int64_t)rr * a.N + n] =
                     __float2half_rn(src >= 0 ? tot[jj] * a.act_scales[src] : 0.f);
@@ -262,56 +270,68 @@ __device__ __forceinline__ void compute_item(const StreamArgs& a, const Smem& sm
     }
 }
 
-__global__ void __launch_bounds__(kWarps * 32, 2) w4_stream_kernel(const StreamArgs a) {
-    __shared__ __align__(16) Smem sm;
+__global__ void __launch_bounds__(kStreamThreads, 1)
+w4_stream_kernel(const StreamArgs a, const __grid_constant__ CUtensorMap tmw) {
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte alignment by offsetting the __shared__ array itself (a round trip through an
+    // integer would lose the shared address space and turn every access into a generic one)
+    StreamSmem& sm = *reinterpret_cast<StreamSmem*>(
+        smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    volatile int* bad = &sm.bad;
     const int P_valid = a.ntp ? min(a.ntp[0], a.P) : a.P;
     const int per_b = a.ks_n * a.rg_n;
     const int total = ((P_valid + 7) / 8) * per_b;
-    // Static round-robin schedule: this CTA's i-th item is blockIdx.x + i * gridDim.x.
-    const int stride = gridDim.x;
-    int item = blockIdx.x;
-    if (item >= total) return;
-    if (warp == 0) {
-        meta_publish(a, meta_issue(a, item, total, per_b, P_valid), total, per_b, sm.meta[0]);
-        meta_publish(a, meta_issue(a, item + stride, total, per_b, P_valid), total, per_b,
-                     sm.meta[1]);
+    if ((int)blockIdx.x >= total) return;
+    if (threadIdx.x == 0) {
+        sm.bad = 0;
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&sm.full[s], 1 + 32);  // producer lane 0 (+ tx bytes) and 32 cp.async arrivals
+            mbar_init(&sm.empty[s], kWarps);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    WeightRegs r0, r1;
-    if (sm.meta[0].any) {
-        load_weights(a, sm.meta[0], warp, lane, r0);
-        stage_item(a, sm, sm.meta[0], 0);
-    }
-    // Iteration i computes item i (shared buffer i%2, meta slot i%3, registers r[i%2]); it first
-    // issues item i+1's loads and warp 0 prepares item i+2's metadata. One barrier per item:
-    // it publishes item i's staged tile and item i+1's metadata, and retires item i-1's buffer.
-    int i = 0;
-    while (true) {
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-            const int buf = half;
-            cp_async_wait_all();
-            __syncthreads();
-            const ItemMeta& cur = sm.meta[i % 3];
-            const ItemMeta& nxt = sm.meta[(i + 1) % 3];
-            const bool has_next = nxt.item < total;
-            if (has_next && nxt.any) {  // empty items stage nothing (their expert may be -1)
-                load_weights(a, nxt, warp, lane, half == 0 ? r1 : r0);
-                stage_item(a, sm, nxt, buf ^ 1);
+    uint32_t st = 0, ph = 0;
+    if (warp == kWarps) {
+        // ---------------- producer ----------------
+        ItemRoute rt = fetch_route(a, blockIdx.x, per_b, P_valid, total);
+        for (int item = blockIdx.x; item < total; item += gridDim.x) {
+            const ItemRoute nx = fetch_route(a, item + gridDim.x, per_b, P_valid, total);
+            if (lane == 0) mbar_wait(&sm.empty[st], ph ^ 1, bad);
+            __syncwarp();
+            produce_item(a, sm, &tmw, item, per_b, P_valid, (int)st, rt);
+            rt = nx;
+            if (++st == kStages) {
+                st = 0;
+                ph ^= 1;
             }
-            MetaRegs mr{};
-            if (warp == 0) mr = meta_issue(a, item + 2 * stride, total, per_b, P_valid);
-            compute_item(a, sm, cur, buf, warp, lane, half == 0 ? r0 : r1);
-            if (warp == 0) meta_publish(a, mr, total, per_b, sm.meta[(i + 2) % 3]);
-            item += stride;
-            ++i;
-            if (!has_next) {
-                cp_async_wait_all();
-                return;
+        }
+        // the compute warps consume every stage issued, so no copy outlives the CTA unless a
+        // wait gave up; then wait (boundedly) for the last stages to land
+        if (*bad && lane == 0) {
+            const uint64_t t0 = global_ns();
+            for (int s = 0; s < kStages; ++s)
+                while (!mbar_try(&sm.full[s], ph ^ (s < (int)st ? 0u : 1u)) &&
+                       global_ns() - t0 < kWaitLimitNs) {
+                }
+        }
+    } else {
+        // ---------------- compute warps ----------------
+        for (int item = blockIdx.x; item < total; item += gridDim.x) {
+            mbar_wait(&sm.full[st], ph, bad);
+            __syncwarp();
+            compute_item(a, sm, (int)st, warp, lane, P_valid);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.empty[st]);
+            if (++st == kStages) {
+                st = 0;
+                ph ^= 1;
             }
         }
     }
+    __syncthreads();
+    if (threadIdx.x == 0 && sm.bad && a.counter) atomicOr(a.counter, 2);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -388,7 +408,10 @@ __device__ void quant_operand_row(const __half* src, int64_t K, int64_t row, con
             out.y = *reinterpret_cast<const uint32_t*>(&d15);
             out.z = h26;
             out.w = *reinterpret_cast<const uint32_t*>(&d37);
-            if (o.xh) reinterpret_cast<uint4*>(o.xh + row * K)[i] = out;
+            // stored in the stream kernel's shared order (act_off): within each 64-chunk block
+            // the unit bits of chunks with bit 3 set are swapped pairwise
+            if (o.xh)
+                reinterpret_cast<uint4*>(o.xh + row * K)[(i & ~int64_t(3)) | ((i & 3) ^ ((i >> 3) & 1))] = out;
             const float2 f04 = __half22float2(*reinterpret_cast<const __half2*>(&h04));
             const float2 f26 = __half22float2(*reinterpret_cast<const __half2*>(&h26));
             const float2 f15 = __half22float2(*reinterpret_cast<const __half2*>(&h15));
@@ -505,7 +528,15 @@ int launch_w4_stream(StreamArgs a, cudaStream_t stream) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    w4_stream_kernel<<<sms * 2, kWarps * 32, 0, stream>>>(a);
+    CUtensorMap tmw;
+    if (!make_tma_map_u8(&tmw, a.w, (uint64_t)a.E * a.N, (uint64_t)a.K / 2, 128, kRowsPerItem,
+                         CU_TENSOR_MAP_SWIZZLE_128B))
+        return set_error("stream path: tensor map encoding failed");
+    const size_t smem = sizeof(StreamSmem) + 1024;
+    cudaError_t ce = cudaFuncSetAttribute(w4_stream_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (ce != cudaSuccess) return (int)ce;
+    w4_stream_kernel<<<sms, kStreamThreads, smem, stream>>>(a, tmw);
     if (int rc = launch_status()) return rc;
     if (a.force_part) {
         const size_t smem = a.mode == kStreamSiluQuant ? (size_t)(a.N / 2) * 2 : 0;
