@@ -365,10 +365,9 @@ def dominant_kernel(torch, args, world, dist, dev, x, ids, w13, s13, z13, E_tota
 
 # dram__bytes_read.sum + dram__bytes_write.sum of the gate_up w4_stream_kernel launch in the
 # committed ncu capture (profiles/w4_stream_kernel_decode.md).
-STREAM_KERNEL_TRAFFIC = 185_420_544 + 4_915_968
-# The same for the prefill gate_up w4_tc_kernel launch (profiles/w4_tc_kernel_prefill.md);
-# None until that capture exists.
-TC_KERNEL_TRAFFIC = None
+STREAM_KERNEL_TRAFFIC = 176_738_816 + 6_138_880
+# The same for the prefill gate_up w4_tc_kernel launch (profiles/w4_tc_kernel_prefill.md).
+TC_KERNEL_TRAFFIC = 281_946_624 + 39_258_368
 
 
 def end_to_end(torch, dist, args, world, dev, x_np, ids_np, w_np, layer, run_grouped_moe,
@@ -492,6 +491,27 @@ def run_reference(args):
     print(json.dumps(res))
 
 
+def profile_op(args):
+    """Run only the dominant op (the gate_up launch the roofline times) `--steps` times on one
+    GPU, for an ncu capture of w4_stream_kernel (decode) or w4_tc_kernel (prefill) on the same
+    inputs as the bench, without the rest of the bench around it."""
+    import torch
+    import w4a8_fp8_wmma as w4
+    dev = torch.device("cuda", 0)
+    cfg = workload_config(args.workload)
+    x_np, ids_np, _ = make_tokens(cfg["T"], cfg["zipf"], cfg["seed"] * 1000)
+    x = torch.from_numpy(x_np).to(dev)
+    ids = torch.from_numpy(ids_np).to(dev)
+    w13, s13, z13, _, _, _ = make_layer(torch, dev, 1000, E_ROUTED + 1)
+    block_m, kern = (128, 6) if args.workload == "prefill" else (8, 7)
+    s, e, n = w4.moe_align_block_size(ids, block_m, E_ROUTED + 1)
+    for _ in range(args.steps):
+        torch.ops.w4a8_b200.moe_gemm1_silu(x, w13, s13, z13, s, e, n, ids.size(1), block_m,
+                                           kern, False)
+    torch.cuda.synchronize()
+    print(f"profile-op {args.workload}: {args.steps} launches of the gate_up op", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -501,10 +521,14 @@ def main():
     ap.add_argument("--workload", choices=["decode", "prefill"], default="decode")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-op", action="store_true",
+                    help="only launch the gate_up op --steps times (for an ncu capture)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.profile_op:
+        profile_op(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

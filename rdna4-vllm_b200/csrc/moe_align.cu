@@ -10,7 +10,8 @@
 //      the padded counts into `offsets` (workspace), expert_ids per block, the tail fill.
 //   2. align_place_kernel (one warp per local expert): each warp walks the slot list in order
 //      with __ballot_sync and writes its expert's slots at offsets[e] + running rank, which is
-//      stable by construction; then the warp writes its padding sentinels.
+//      stable by construction. For many slots (prefill) align_place_chunked_kernel ranks
+//      2048-slot chunks in parallel instead. The padding sentinels come from the count kernel.
 // The slot list is staged in shared memory as int16 local expert ids when it fits.
 #include "common.cuh"
 #include "internal.h"
@@ -61,10 +62,12 @@ align_count_kernel(const int32_t* __restrict__ topk_ids, int64_t num_slots, int 
         __syncthreads();
     }
     int32_t run = partial[tid] - local;  // exclusive prefix of this thread's chunk
+    const int32_t sentinel = (int32_t)num_slots;
     for (int e = e0; e < e1; ++e) {
         offsets[e] = run;
         const int32_t padded = (counts[e] + block_m - 1) / block_m * block_m;
         for (int32_t b = run / block_m; b < (run + padded) / block_m; ++b) expert_ids[b] = e;
+        for (int32_t p = run + counts[e]; p < run + padded; ++p) sorted_ids[p] = sentinel;
         run += padded;
     }
     const int32_t total = partial[kCountThreads - 1];
@@ -72,7 +75,6 @@ align_count_kernel(const int32_t* __restrict__ topk_ids, int64_t num_slots, int 
         offsets[num_local] = total;
         ntp_out[0] = total;
     }
-    const int32_t sentinel = (int32_t)num_slots;
     for (int64_t i = total + tid; i < capacity; i += kCountThreads) sorted_ids[i] = sentinel;
     for (int64_t b = total / block_m + tid; b < capacity / block_m; b += kCountThreads)
         expert_ids[b] = -1;
@@ -94,7 +96,6 @@ align_place_kernel(const int32_t* __restrict__ topk_ids, int64_t num_slots, int 
     const int e = blockIdx.x * kPlaceWarps + (threadIdx.x >> 5);
     if (e >= num_local) return;
     const int32_t base = offsets[e];
-    const int32_t end = offsets[e + 1];
     const uint32_t lt = (1u << lane) - 1u;
     int32_t run = base;
     for (int64_t c = 0; c < num_slots; c += 32) {
@@ -109,8 +110,67 @@ align_place_kernel(const int32_t* __restrict__ topk_ids, int64_t num_slots, int 
         }
         run += __popc(m);
     }
-    const int32_t sentinel = (int32_t)num_slots;
-    for (int32_t p = run + lane; p < end; p += 32) sorted_ids[p] = sentinel;
+}
+
+// Chunked stable placement, for many slots and up to kChunkMaxExperts local experts. CTA c
+// owns slots [c*kChunk, (c+1)*kChunk). It counts each expert's slots in the chunks before it
+// (shared-memory histogram), then ranks its own slots in rounds of 1024 in slot order:
+// __match_any_sync gives the rank among equal experts inside a warp, and a per-expert
+// exclusive scan over the 32 warps gives the warp's offset. The padding sentinels are written
+// by the count kernel.
+constexpr int kChunk = 2048;
+constexpr int kChunkThreads = 1024;
+constexpr int kChunkMaxExperts = 512;
+__global__ void __launch_bounds__(kChunkThreads)
+align_place_chunked_kernel(const int32_t* __restrict__ topk_ids, int64_t num_slots,
+                           int num_experts, int num_local, const int32_t* __restrict__ expert_map,
+                           const int32_t* __restrict__ offsets, int32_t* __restrict__ sorted_ids,
+                           int32_t* __restrict__ slot_to_row) {
+    extern __shared__ int32_t csm[];
+    int32_t* base = csm;                          // [num_local] running position per expert
+    int32_t* tot = base + num_local;              // [num_local] count in the current round
+    int32_t* wcnt = tot + num_local;              // [32][num_local] per-warp counts -> prefixes
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t c0 = (int64_t)blockIdx.x * kChunk;
+    const int64_t c1 = c0 + kChunk < num_slots ? c0 + kChunk : num_slots;
+    for (int e = tid; e < num_local; e += kChunkThreads) base[e] = 0;
+    __syncthreads();
+    for (int64_t i = tid; i < c0; i += kChunkThreads) {
+        const int le = local_expert(topk_ids, expert_map, i, num_experts);
+        if (le >= 0 && le < num_local) atomicAdd(&base[le], 1);
+    }
+    __syncthreads();
+    for (int e = tid; e < num_local; e += kChunkThreads) base[e] += offsets[e];
+    const uint32_t lt = (1u << lane) - 1u;
+    for (int64_t r0 = c0; r0 < c1; r0 += kChunkThreads) {
+        for (int e = tid; e < 32 * num_local; e += kChunkThreads) wcnt[e] = 0;
+        __syncthreads();
+        const int64_t i = r0 + tid;
+        int le = -1;
+        if (i < c1) le = local_expert(topk_ids, expert_map, i, num_experts);
+        if (le >= num_local) le = -1;
+        const uint32_t peers = __match_any_sync(0xffffffffu, le);
+        const int rank = __popc(peers & lt);
+        if (le >= 0 && rank == 0) wcnt[warp * num_local + le] = __popc(peers);
+        __syncthreads();
+        for (int e = tid; e < num_local; e += kChunkThreads) {  // exclusive scan over warps
+            int32_t run = 0;
+            for (int w = 0; w < 32; ++w) {
+                const int32_t v = wcnt[w * num_local + e];
+                wcnt[w * num_local + e] = run;
+                run += v;
+            }
+            tot[e] = run;
+        }
+        __syncthreads();
+        if (le >= 0) {
+            const int32_t pos = base[le] + wcnt[warp * num_local + le] + rank;
+            sorted_ids[pos] = (int32_t)i;
+            if (slot_to_row) slot_to_row[i] = pos;
+        }
+        __syncthreads();
+        for (int e = tid; e < num_local; e += kChunkThreads) base[e] += tot[e];
+    }
 }
 
 }  // namespace
@@ -155,6 +215,18 @@ int launch_moe_align(const int32_t* topk_ids, int64_t num_slots, int32_t num_exp
         sorted_token_ids, sorted_capacity, expert_ids, num_tokens_post_padded, offsets);
     int st = launch_status();
     if (st) return st;
+    if (num_slots > 4 * kChunk && num_local_experts <= kChunkMaxExperts) {
+        const size_t smem = (size_t)34 * num_local_experts * sizeof(int32_t);
+        cudaError_t ce = cudaFuncSetAttribute(align_place_chunked_kernel,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)smem);
+        if (ce != cudaSuccess) return (int)ce;
+        const unsigned grid = (unsigned)((num_slots + kChunk - 1) / kChunk);
+        align_place_chunked_kernel<<<grid, kChunkThreads, smem, stream>>>(
+            topk_ids, num_slots, num_experts, num_local_experts, expert_map, offsets,
+            sorted_token_ids, slot_to_row);
+        return launch_status();
+    }
     const dim3 grid((num_local_experts + kPlaceWarps - 1) / kPlaceWarps);
     if (num_slots <= kMaxSmemSlots) {
         const size_t smem = align_up((size_t)num_slots * sizeof(int16_t), 16);
