@@ -318,8 +318,8 @@ def dominant_kernel(torch, args, world, dist, dev, x, ids, w13, s13, z13, E_tota
     decode: the grouped GEMV op (operand quant + w4_stream_kernel + SiLU finish), HBM-bound;
     algorithmic bytes = touched experts' w13 bytes (codes + scales + zeros) + the fp16
     activations read + the fp16 SiLU rows written.
-    prefill: the tcgen05 tile op (operand quant + sorted-row gather + w4_tc_kernel with the
-    fused SiLU epilogue), tensor-bound; algorithmic FLOPs = 2 * routed rows * 2*inter * hidden
+    prefill: the tcgen05 tile op (tc_quant_rows_kernel, which quantises into sorted order, +
+    w4_tc_kernel with the fused SiLU epilogue), tensor-bound; algorithmic FLOPs = 2 * routed rows * 2*inter * hidden
     (padding rows not counted); peak = the dense e4m3 rate, twice the measured bf16 GEMM rate."""
     hbm, fp8_peak, src = peaks()
     import w4a8_fp8_wmma as w4
@@ -344,7 +344,7 @@ def dominant_kernel(torch, args, world, dist, dev, x, ids, w13, s13, z13, E_tota
     if prefill:
         flops = 2.0 * rows * 2 * INTER * H
         ach = flops / (ms / 1e3) / 1e12
-        return {"kernel": "gate_up tile op: operand_quant + tc_gather + w4_tc_kernel (SiLU epilogue)",
+        return {"kernel": "gate_up tile op: tc_quant_rows_kernel + w4_tc_kernel (SiLU epilogue)",
                 "bound": "tensor", "achieved": round(ach, 1), "peak": round(fp8_peak, 1),
                 "unit": "TFLOP/s", "frac": round(ach / fp8_peak, 4),
                 "peak_source": f"{src} (e4m3 dense = 2 x measured bf16)",
@@ -365,9 +365,9 @@ def dominant_kernel(torch, args, world, dist, dev, x, ids, w13, s13, z13, E_tota
 
 # dram__bytes_read.sum + dram__bytes_write.sum of the gate_up w4_stream_kernel launch in the
 # committed ncu capture (profiles/w4_stream_kernel_decode.md).
-STREAM_KERNEL_TRAFFIC = 176_738_816 + 6_138_880
+STREAM_KERNEL_TRAFFIC = 176_702_208 + 6_877_696
 # The same for the prefill gate_up w4_tc_kernel launch (profiles/w4_tc_kernel_prefill.md).
-TC_KERNEL_TRAFFIC = 281_946_624 + 39_258_368
+TC_KERNEL_TRAFFIC = 305_600_512 + 45_892_096
 
 
 def end_to_end(torch, dist, args, world, dev, x_np, ids_np, w_np, layer, run_grouped_moe,
