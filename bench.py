@@ -169,15 +169,10 @@ def run_ours(args):
         ids_r = ids[:, :TOP_K].contiguous()
         tw_r = tw[:, :TOP_K].contiguous()
         recorded = {}
-        base_fn = layer.expert_fn
-
-        def recording_fn(rows, lid):
-            recorded["rows"], recorded["ids"] = rows, lid
-            return base_fn(rows, lid)
-        layer.expert_fn = recording_fn
 
         def step_fn():
             holder["y"] = layer(x, ids_r, tw_r)
+            recorded["rows"], recorded["ids"] = layer.last_recv
     else:
         layer = None
         w13, s13, z13, w2, s2, z2 = make_layer(torch, dev, 1000, E_total)
@@ -289,11 +284,12 @@ def _max_over_ranks(torch, dist, world, dev, v):
 def launches_per_step(workload: str, world: int) -> int:
     """Kernels of this library per step: decode = align count + place, operand quant, gate_up
     GEMV + finish, down GEMV, gather-reduce (7); prefill = align count + place, then per GEMM
-    operand quant + sorted-row gather + w4_tc_kernel (2 x 3), inverse map + gather-reduce (10).
-    EP adds the shared expert's 7 and the combine gather-reduce."""
-    n = 7 if workload == "decode" else 10
+    tc_quant_rows + w4_tc_kernel (2 x 2), inverse map + gather-reduce (8). EP runs the decode
+    layer once on the received rows plus the rank's own tokens (the shared expert rides along)
+    and adds the combine gather-reduce (8)."""
+    n = 7 if workload == "decode" else 8
     if world > 1:
-        n += 8
+        n += 1
     return n
 
 

@@ -60,6 +60,20 @@ class ExpertParallelMoE:
         self.w = (w13, s13, z13, w2, s2, z2)
         self.shared = shared  # (w13, s13, z13, w2, s2, z2) of one replicated shared expert
         self.expert_fn = expert_fn or self._gpu_experts
+        # With the built-in GPU experts the shared expert rides the routed call as local expert
+        # E_loc: its weights are appended once here, and the rank's own tokens join the received
+        # rows with that id, so a step runs one layer call instead of two.
+        self._fused_shared = expert_fn is None and shared is not None and w13 is not None
+        if self._fused_shared:
+            cat = []
+            for i, (t_r, t_s) in enumerate(zip(self.w, shared)):
+                if t_r is None or t_r.numel() == 0:
+                    if not (t_s is None or t_s.numel() == 0):
+                        raise ValueError("routed and shared experts disagree on zero points")
+                    cat.append(t_r)
+                else:
+                    cat.append(torch.cat([t_r, t_s], 0).contiguous())
+            self.w_all = tuple(cat)
         self._ntp = {}  # cached device scalars (no host->device copies inside graph capture)
 
     # ---- compute on received rows ------------------------------------------------------
@@ -99,7 +113,21 @@ class ExpertParallelMoE:
         recv_id = torch.empty_like(send_id)
         dist.all_to_all_single(recv_x, send_x, group=self.group)
         dist.all_to_all_single(recv_id, send_id, group=self.group)
-        y = self.expert_fn(recv_x, recv_id).to(x.dtype).contiguous()  # (W*C, H)
+        self.last_recv = (recv_x, recv_id)  # for profiling tools: this step's received rows
+        sh = None
+        if self._fused_shared:
+            w13, s13, z13, w2, s2, z2 = self.w_all
+            rows = torch.cat([recv_x, x], 0)
+            ids = torch.cat([recv_id, torch.full((T,), self.E_loc, dtype=torch.int32, device=dev)])
+            ids = ids.view(-1, 1)
+            valid = ids >= 0
+            ids = torch.where(valid, ids, torch.full_like(ids, self.E_loc + 1))  # skipped
+            y_all = torch.ops.w4a8_b200.moe_decode(rows, w13, s13, z13, w2, s2, z2,
+                                                   valid.to(torch.float32), ids)
+            y = y_all[:W * C].to(x.dtype).contiguous()
+            sh = y_all[W * C:]
+        else:
+            y = self.expert_fn(recv_x, recv_id).to(x.dtype).contiguous()  # (W*C, H)
         back = torch.empty_like(y)
         dist.all_to_all_single(back, y, group=self.group)
         # Row `row[s]` of `back` holds slot s; empty rows carry the sentinel T*k.
@@ -117,7 +145,8 @@ class ExpertParallelMoE:
             for j in range(k):
                 s = torch.arange(T) * k + j
                 out += tw[s, None] * back[row[s]].to(torch.float32)
-        sh = self._shared(x)
+        if not self._fused_shared:
+            sh = self._shared(x)
         if sh is not None:
             out = out + sh.to(torch.float32)
         return out
