@@ -201,6 +201,28 @@ W4A8_API int w4a8_silu_and_mul(const void* x, void* out, int64_t M, int64_t inte
                                w4a8_stream_t stream);
 
 /*
+ * Expert-parallel dispatch (no counterpart in the reference, which has no expert parallelism;
+ * its expert_map is only forwarded to vLLM's align, w4a8_fp8_wmma/w4a8_fp8_wmma/
+ * moe_experts.py:587-589). Slot s = t*top_k + j goes to rank d = topk_ids[s] / experts_per_rank
+ * (clamped to [0, world)) at send row d*capacity + (number of earlier slots bound for d):
+ * send_x[row] = x[t] (fp16, H), send_id[row] = topk_ids[s] - d*experts_per_rank (local expert),
+ * slot_row[s] = row. Unclaimed rows get send_id -1. capacity >= T*top_k; graph-capturable.
+ */
+W4A8_API int w4a8_ep_dispatch(const void* x, const int32_t* topk_ids, int64_t T, int64_t top_k,
+                              int64_t H, int32_t experts_per_rank, int32_t world,
+                              int64_t capacity, void* send_x, int32_t* send_id,
+                              int32_t* slot_row, w4a8_stream_t stream);
+
+/*
+ * Expert-parallel combine: out[t, n] = sum_{j ascending} w[t*top_k+j] * back[slot_row[t*top_k+j], n]
+ * (fp32; fp16 back rows), plus fp32(shared[t, n]) when `shared` (fp16 (T, H)) is not NULL.
+ * The arithmetic of mmq_fp8_moe_gather_reduce followed by the shared-expert add.
+ */
+W4A8_API int w4a8_ep_combine(const void* back, const int32_t* slot_row,
+                             const float* topk_weights, const void* shared, float* out,
+                             int64_t T, int64_t top_k, int64_t H, w4a8_stream_t stream);
+
+/*
  * Whole gated MoE layer at decode sizes in one call: moe_align (block 8) -> gate_up GEMV ->
  * silu_and_mul -> down GEMV -> topk-weighted reduce, the decode branch of the reference's
  * composition _run_grouped_moe (w4a8_fp8_wmma/w4a8_fp8_wmma/moe_experts.py:563-648), which

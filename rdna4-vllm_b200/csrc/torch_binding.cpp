@@ -307,6 +307,56 @@ at::Tensor silu_and_mul_forward(const at::Tensor& x) {
     return out;
 }
 
+std::vector<at::Tensor> ep_dispatch_forward(const at::Tensor& x, const at::Tensor& topk_ids,
+                                            int64_t experts_per_rank, int64_t world,
+                                            int64_t capacity) {
+    TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kHalf && x.dim() == 2 && x.is_contiguous(),
+                "x must be a contiguous (T, H) fp16 CUDA tensor");
+    TORCH_CHECK(topk_ids.is_cuda() && topk_ids.scalar_type() == at::kInt &&
+                    topk_ids.is_contiguous() && topk_ids.dim() == 2 &&
+                    topk_ids.size(0) == x.size(0),
+                "topk_ids must be a contiguous (T, top_k) int32 CUDA tensor");
+    const c10::cuda::CUDAGuard guard(x.device());
+    const int64_t T = x.size(0), H = x.size(1), k = topk_ids.size(1);
+    auto send_x = at::empty({world * capacity, H}, x.options());
+    auto send_id = at::empty({world * capacity}, topk_ids.options());
+    auto slot_row = at::empty({T * k}, topk_ids.options());
+    check_status(w4a8_ep_dispatch(x.data_ptr(), topk_ids.data_ptr<int32_t>(), T, k, H,
+                                  (int32_t)experts_per_rank, (int32_t)world, capacity,
+                                  send_x.data_ptr(), send_id.data_ptr<int32_t>(),
+                                  slot_row.data_ptr<int32_t>(), cur_stream()),
+                 "ep_dispatch");
+    return {send_x, send_id, slot_row};
+}
+
+at::Tensor ep_combine_forward(const at::Tensor& back, const at::Tensor& slot_row,
+                              const at::Tensor& topk_weights, const c10::optional<at::Tensor>& shared,
+                              int64_t top_k) {
+    TORCH_CHECK(back.is_cuda() && back.scalar_type() == at::kHalf && back.dim() == 2 &&
+                    back.is_contiguous(),
+                "back must be a contiguous (rows, H) fp16 CUDA tensor");
+    TORCH_CHECK(slot_row.scalar_type() == at::kInt && slot_row.is_contiguous() &&
+                    topk_weights.scalar_type() == at::kFloat && topk_weights.is_contiguous() &&
+                    topk_weights.numel() == slot_row.numel() && top_k > 0 &&
+                    slot_row.numel() % top_k == 0,
+                "slot_row int32 / topk_weights fp32 must be contiguous with T*top_k entries");
+    const c10::cuda::CUDAGuard guard(back.device());
+    const int64_t T = slot_row.numel() / top_k, H = back.size(1);
+    const void* sh = nullptr;
+    if (shared.has_value() && shared->defined()) {
+        TORCH_CHECK(shared->scalar_type() == at::kHalf && shared->is_contiguous() &&
+                        shared->size(0) == T && shared->size(1) == H,
+                    "shared must be a contiguous (T, H) fp16 tensor");
+        sh = shared->data_ptr();
+    }
+    auto out = at::empty({T, H}, back.options().dtype(at::kFloat));
+    check_status(w4a8_ep_combine(back.data_ptr(), slot_row.data_ptr<int32_t>(),
+                                 topk_weights.data_ptr<float>(), sh, out.data_ptr<float>(), T,
+                                 top_k, H, cur_stream()),
+                 "ep_combine");
+    return out;
+}
+
 at::Tensor moe_decode_forward(const at::Tensor& x, const at::Tensor& w13, const at::Tensor& s13,
                               const at::Tensor& z13, const at::Tensor& w2, const at::Tensor& s2,
                               const at::Tensor& z2, const at::Tensor& topk_weights,
@@ -394,6 +444,8 @@ TORCH_LIBRARY_IMPL(w4a8_fp8_wmma, CUDA, m) {
 TORCH_LIBRARY(w4a8_b200, m) {
     m.def("act_quant_fp8(Tensor x) -> Tensor[]");
     m.def("silu_and_mul(Tensor x) -> Tensor");
+    m.def("ep_dispatch(Tensor x, Tensor topk_ids, int experts_per_rank, int world, int capacity) -> Tensor[]");
+    m.def("ep_combine(Tensor back, Tensor slot_row, Tensor topk_weights, Tensor? shared, int top_k) -> Tensor");
     // Whole gated MoE layer at decode sizes (align -> gate_up+SiLU -> down -> reduce).
     m.def("moe_decode(Tensor x, Tensor w13, Tensor s13, Tensor z13, Tensor w2, Tensor s2, "
           "Tensor z2, Tensor topk_weights, Tensor topk_ids) -> Tensor");
@@ -408,6 +460,8 @@ TORCH_LIBRARY(w4a8_b200, m) {
 TORCH_LIBRARY_IMPL(w4a8_b200, CUDA, m) {
     m.impl("act_quant_fp8", &act_quant_fp8_forward);
     m.impl("silu_and_mul", &silu_and_mul_forward);
+    m.impl("ep_dispatch", &ep_dispatch_forward);
+    m.impl("ep_combine", &ep_combine_forward);
     m.impl("moe_decode", &moe_decode_forward);
     m.impl("moe_gemm1_silu", &gemm1_silu_impl);
     m.impl("moe_align_block_size", &moe_align_block_size_forward);

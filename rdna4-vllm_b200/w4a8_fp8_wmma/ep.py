@@ -15,7 +15,10 @@ per-rank layer. Rank r of W owns routed experts [r*E/W, (r+1)*E/W) and its own t
      the source applies its routing weights with the gather-reduce op (slot order) and adds
      the replicated shared expert, if any.
 
-The collectives use torch.distributed (NCCL on GPUs, gloo for the CPU tests). `expert_fn`
+On GPUs steps 1 and 3 are the library's ep_dispatch / ep_combine kernels (stable positions and
+row copies in one launch; the slot-order reduce plus the shared-expert add in one launch), and
+the shared expert joins the routed layer call as local expert E_loc. The collectives use
+torch.distributed (NCCL on GPUs, gloo for the CPU tests). `expert_fn`
 makes the compute step pluggable so the permutation logic is testable on CPU ranks.
 """
 from __future__ import annotations
@@ -99,6 +102,8 @@ class ExpertParallelMoE:
                 topk_weights: torch.Tensor) -> torch.Tensor:
         """x (T, H) fp16 local tokens; topk_ids/weights (T, top_k) with GLOBAL expert ids.
         Returns (T, H) fp32: the routed experts' weighted sum plus the shared expert."""
+        if x.is_cuda:
+            return self._forward_cuda(x, topk_ids, topk_weights)
         T, H = x.shape
         k = topk_ids.size(1)
         W, C = self.world, T * k
@@ -113,42 +118,60 @@ class ExpertParallelMoE:
         recv_id = torch.empty_like(send_id)
         dist.all_to_all_single(recv_x, send_x, group=self.group)
         dist.all_to_all_single(recv_id, send_id, group=self.group)
+        y = self.expert_fn(recv_x, recv_id).to(x.dtype).contiguous()  # (W*C, H)
+        back = torch.empty_like(y)
+        dist.all_to_all_single(back, y, group=self.group)
+        # row `row[s]` of `back` holds slot s
+        tw = topk_weights.reshape(-1).to(torch.float32).contiguous()
+        # CPU ranks (tests): slot-order weighted sum, as the GPU combine kernel computes it
+        out = torch.zeros((T, H), dtype=torch.float32)
+        for j in range(k):
+            s = torch.arange(T) * k + j
+            out += tw[s, None] * back[row[s]].to(torch.float32)
+        sh = self._shared(x)
+        if sh is not None:
+            out = out + sh.to(torch.float32)
+        return out
+
+    def _const(self, name: str, n: int, value, dtype, dev) -> torch.Tensor:
+        """Cached constant device tensors (no host->device copies inside graph capture)."""
+        key = (name, n, dev)
+        if key not in self._ntp:
+            self._ntp[key] = torch.full((n,), value, dtype=dtype, device=dev)
+        return self._ntp[key]
+
+    def _forward_cuda(self, x, topk_ids, topk_weights):
+        """GPU path: the dispatch and combine kernels around the NCCL all-to-alls; with the
+        built-in experts one decode-layer call serves the received rows and, as local expert
+        E_loc, the replicated shared expert on this rank's own tokens."""
+        T, H = x.shape
+        k = topk_ids.size(1)
+        W, C = self.world, T * k
+        dev = x.device
+        send_x, send_id, slot_row = torch.ops.w4a8_b200.ep_dispatch(
+            x.contiguous(), topk_ids.to(torch.int32).contiguous(), self.E_loc, W, C)
+        recv_x = torch.empty_like(send_x)
+        recv_id = torch.empty_like(send_id)
+        dist.all_to_all_single(recv_x, send_x, group=self.group)
+        dist.all_to_all_single(recv_id, send_id, group=self.group)
         self.last_recv = (recv_x, recv_id)  # for profiling tools: this step's received rows
         sh = None
         if self._fused_shared:
             w13, s13, z13, w2, s2, z2 = self.w_all
             rows = torch.cat([recv_x, x], 0)
-            ids = torch.cat([recv_id, torch.full((T,), self.E_loc, dtype=torch.int32, device=dev)])
-            ids = ids.view(-1, 1)
-            valid = ids >= 0
-            ids = torch.where(valid, ids, torch.full_like(ids, self.E_loc + 1))  # skipped
+            ids = torch.cat([recv_id, self._const("shared_id", T, self.E_loc, torch.int32, dev)])
+            ones = self._const("ones", W * C + T, 1.0, torch.float32, dev)
+            # id -1 (unclaimed row) is outside [0, E_loc + 1): the layer skips it
             y_all = torch.ops.w4a8_b200.moe_decode(rows, w13, s13, z13, w2, s2, z2,
-                                                   valid.to(torch.float32), ids)
-            y = y_all[:W * C].to(x.dtype).contiguous()
-            sh = y_all[W * C:]
+                                                   ones.view(-1, 1), ids.view(-1, 1))
+            y, sh = y_all[:W * C], y_all[W * C:]
         else:
             y = self.expert_fn(recv_x, recv_id).to(x.dtype).contiguous()  # (W*C, H)
+            sh = self._shared(x)
         back = torch.empty_like(y)
         dist.all_to_all_single(back, y, group=self.group)
-        # Row `row[s]` of `back` holds slot s; empty rows carry the sentinel T*k.
-        sorted_ids = torch.full((W * C,), T * k, dtype=torch.int32, device=dev)
-        sorted_ids[row] = slots.to(torch.int32)
         tw = topk_weights.reshape(-1).to(torch.float32).contiguous()
-        if back.is_cuda:
-            key = (W * C, dev)
-            if key not in self._ntp:
-                self._ntp[key] = torch.full((1,), W * C, dtype=torch.int32, device=dev)
-            ntp = self._ntp[key]
-            out = torch.ops.w4a8_fp8_wmma.mmq_fp8_moe_gather_reduce(back, sorted_ids, tw, ntp, k)
-        else:  # CPU ranks (tests): same slot-order weighted sum
-            out = torch.zeros((T, H), dtype=torch.float32)
-            for j in range(k):
-                s = torch.arange(T) * k + j
-                out += tw[s, None] * back[row[s]].to(torch.float32)
-        if not self._fused_shared:
-            sh = self._shared(x)
-        if sh is not None:
-            out = out + sh.to(torch.float32)
-        return out
+        return torch.ops.w4a8_b200.ep_combine(back, slot_row, tw,
+                                              None if sh is None else sh.contiguous(), k)
 
     __call__ = forward
