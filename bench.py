@@ -286,10 +286,10 @@ def launches_per_step(workload: str, world: int) -> int:
     GEMV + finish, down GEMV, gather-reduce (7); prefill = align count + place, then per GEMM
     tc_quant_rows + w4_tc_kernel (2 x 2), inverse map + gather-reduce (8). EP runs the decode
     layer once on the received rows plus the rank's own tokens (the shared expert rides along)
-    and adds the combine gather-reduce (8)."""
+    and adds the ep_dispatch and ep_combine kernels (9)."""
     n = 7 if workload == "decode" else 8
     if world > 1:
-        n += 1
+        n += 2
     return n
 
 
