@@ -369,3 +369,34 @@ def test_silu_and_mul_exhaustive_fp16_gate(w4):
         gf = g.float()
         ref = (gf / (1.0 + torch.exp(-gf))).to(torch.float16) * torch.tensor(up, dtype=torch.float16, device="cuda")
         assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+
+
+def test_ep_dispatch_and_combine_kernels_vs_torch(w4):
+    """ep_dispatch / ep_combine against the torch statement of the same plan (plan_dispatch +
+    index copies + slot-order reduce): rows, local ids and slot rows are integer work and must
+    match exactly; the combine must equal the slot-order fmul/fadd sum plus the shared add."""
+    from w4a8_fp8_wmma.ep import plan_dispatch
+    T, k, H, E, W = 24, 4, 256, 64, 4
+    rng = np.random.default_rng(77)
+    ids = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
+    x = rng.standard_normal((T, H), dtype=np.float32).astype(np.float16)
+    C = T * k
+    xd, idd = cu(x), cu(ids)
+    send_x, send_id, slot_row = torch.ops.w4a8_b200.ep_dispatch(xd, idd, E // W, W, C)
+    dest, pos, row = plan_dispatch(idd, E // W, W, C)
+    assert torch.equal(slot_row.long(), row)
+    ref_id = torch.full((W * C,), -1, dtype=torch.int32, device="cuda")
+    ref_id[row] = (idd.reshape(-1).long() - dest * (E // W)).int()
+    assert torch.equal(send_id, ref_id)
+    slots = torch.arange(T * k, device="cuda")
+    assert torch.equal(send_x[row], xd[slots // k])
+    back = torch.randn((W * C, H), device="cuda").half()
+    tw = torch.rand(T * k, device="cuda")
+    sh = torch.randn((T, H), device="cuda").half()
+    out = torch.ops.w4a8_b200.ep_combine(back, slot_row, tw, sh, k)
+    ref = torch.zeros((T, H), device="cuda")
+    for j in range(k):
+        s = torch.arange(T, device="cuda") * k + j
+        ref = ref + tw[s, None] * back[row[s]].float()
+    ref = ref + sh.float()
+    assert torch.equal(out, ref)
