@@ -50,9 +50,6 @@ namespace w4a8 {
 
 namespace {
 
-#ifndef W4A8_TC_DEFER
-#define W4A8_TC_DEFER 0
-#endif
 constexpr int kTcThreads = 512;
 constexpr int kFoldWarps = 8;
 
@@ -475,12 +472,12 @@ w4_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmw,
             }
         }
     } else if (warp >= 8) {
-        // ---------------- fold + deferred epilogue ----------------
+        // ---------------- fold + epilogue ----------------
         // Warp w folds TMEM lane quadrant w % 4, columns [h * kCols, (h + 1) * kCols). Warp 8's
         // lane 0 waits for the group's sums and accumulator; a named barrier releases the rest.
-        // A finished tile goes to a shared fp16 tile (double buffered); its SiLU / stores are
-        // spread over the K-groups of the CTA's next tile (slice g of G per group), where they
-        // fill the fold warps' waits, and flushed after the last tile.
+        // A finished tile goes to a shared fp16 tile, double buffered so that a warp may park
+        // the next tile while others still store this one; all fold warps then write it out
+        // row-contiguously (SiLU(gate) * up for the fused op).
         constexpr int kCols = C::kCols;
         const int q = warp & 3;
         const int fw = warp - 8;
@@ -489,9 +486,10 @@ w4_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmw,
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
         RingPos<C::kSStages> ss;
         RingPos<C::kAcc> tb;
-        int pend_buf = -1, pend_r0 = 0, pend_mt = 0, tiles_done = 0;
-        // columns [c_lo, c_hi) of the pending tile: SiLU(gate) * up, or a copy, to global
-        auto drain = [&](int c_lo, int c_hi) {
+        int tiles_done = 0;
+        // the parked tile (buffer pend_buf, rows r0.., weight tile mt) to global memory
+        auto drain = [&](int pend_buf, int pend_r0, int pend_mt) {
+            const int c_lo = 0, c_hi = NT;
             const __half* ot = sm.otile[pend_buf];
             if (a.silu) {
                 const int n = pend_mt * 64 + 2 * lane;
@@ -576,9 +574,6 @@ w4_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmw,
                 }
                 ss.next();
                 tb.next();
-#if W4A8_TC_DEFER
-                if (pend_buf >= 0) drain(g * NT / G, (g + 1) * NT / G);
-#endif
             }
             // park the finished tile: fp16(tot * a_scale) into the free shared tile
             const int buf = tiles_done & 1;
@@ -587,16 +582,9 @@ w4_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmw,
                 sm.otile[buf][(c0 + c) * 128 + m] = __float2half_rn(
                     tot[c] * __shfl_sync(0xffffffffu, asc_l[c >> 5], c & 31));
             asm volatile("bar.sync 1, %0;" ::"n"(kFoldWarps * 32) : "memory");
-            pend_buf = buf;
-            pend_r0 = r0;
-            pend_mt = mt;
+            drain(buf, r0, mt);
             ++tiles_done;
-#if !W4A8_TC_DEFER
-            drain(0, NT);
-            pend_buf = -1;
-#endif
         }
-        if (pend_buf >= 0) drain(0, NT);
     }
 
     asm volatile("tcgen05.fence::before_thread_sync;" ::);
