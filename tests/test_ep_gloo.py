@@ -1,4 +1,4 @@
-"""Expert-parallel dispatch/combine on CPU `gloo` ranks (world size 2), with an identity
+"""Expert-parallel dispatch/combine on CPU `gloo` ranks (world sizes 2 and 4), with an identity
 "expert" so the permutation logic is checked exactly; plus host-side failure cases: a rank
 that dies before the exchange and a rank holding the wrong expert shard raise instead of hang.
 """
@@ -36,7 +36,7 @@ def _worker_identity(rank, world, port, q):
         ok_all, count_all = True, True
         for skew in (False, True):
             torch.manual_seed(100 + rank)
-            T, H, E, k = 6, 16, 8, 3
+            T, H, E, k = 6, 16, 16, 3
             x = torch.randn(T, H).to(torch.float16)
             if skew:  # every slot routes to rank 0's experts
                 ids = torch.stack([torch.randperm(E // world)[:k] for _ in range(T)]).to(torch.int32)
@@ -77,8 +77,9 @@ def _spawn(fn, world, *args, reporters=None):
     return sorted(res, key=lambda r: r[0])
 
 
-def test_ep_dispatch_combine_identity_world2():
-    res = _spawn(_worker_identity, 2)
+@pytest.mark.parametrize("world", [2, 4])
+def test_ep_dispatch_combine_identity(world):
+    res = _spawn(_worker_identity, world)
     for rank, ok, count_ok, err in res:
         assert err is None, err
         assert ok and count_ok, (rank, ok, count_ok)

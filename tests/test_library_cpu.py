@@ -112,6 +112,34 @@ def test_align_validation():
     assert "multiple of block_m" in _err(lib)
 
 
+def test_ep_c_abi_validation():
+    lib = load_lib()
+    d = lib.w4a8_ep_dispatch
+    d.restype = ctypes.c_int
+    d.argtypes = [c_vp, c_vp, c_i64, c_i64, c_i64, c_i32, c_i32, c_i64, c_vp, c_vp, c_vp, c_vp]
+    assert d(1, 1, 4, 2, 20, 8, 2, 8, 1, 1, 1, None) == -1          # H % 8 != 0
+    assert "multiple of 8" in _err(lib)
+    assert d(1, 1, 4, 2, 64, 8, 2, 7, 1, 1, 1, None) == -1          # capacity < T * top_k
+    assert "capacity" in _err(lib)
+    assert d(None, None, 0, 2, 64, 8, 2, 0, None, None, None, None) == 0   # T = 0: no-op
+    c = lib.w4a8_ep_combine
+    c.restype = ctypes.c_int
+    c.argtypes = [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp]
+    assert c(1, 1, 1, None, 1, 4, 17, 64, None) == -1              # top_k > 16
+    assert "top_k" in _err(lib)
+    assert c(None, None, None, None, None, 0, 2, 64, None) == 0      # T = 0: no-op
+
+
+def test_silu_and_mul_c_abi_validation():
+    lib = load_lib()
+    f = lib.w4a8_silu_and_mul
+    f.restype = ctypes.c_int
+    f.argtypes = [c_vp, c_vp, c_i64, c_i64, c_vp]
+    assert f(None, None, -1, 4, None) == -1
+    assert "negative" in _err(lib)
+    assert f(None, None, 0, 4, None) == 0
+
+
 # ---------------------------------------------------------------- torch surface ------------
 REF_SCHEMAS = {
     "mmq_fp8_gemm": "mmq_fp8_gemm(Tensor x, Tensor w_packed, Tensor scales, Tensor w_zeros, int kernel, bool weight_is_e2m1=False) -> Tensor",
