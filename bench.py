@@ -55,6 +55,40 @@ def workload_config(name: str):
     return dict(T=32, zipf=False, seed=1)
 
 
+def metric_name(workload: str) -> str:
+    return ("MoE-layer tokens/s (Qwen3.6-35B-A3B-shaped, decode T=32)" if workload == "decode"
+            else "MoE-layer tokens/s (Qwen3.6-35B-A3B-shaped, prefill T=4096)")
+
+
+def base_config(workload: str, world: int, layers: int = 1) -> dict:
+    """The workload description both arms print (the driver compares the two dicts)."""
+    cfg = workload_config(workload)
+    return {"workload": f"configs[{1 if workload == 'decode' else 2}] MoE layer {workload}",
+            "tokens_per_gpu": cfg["T"], "hidden": H, "inter": INTER, "experts": E_ROUTED,
+            "shared_experts": 1, "top_k": TOP_K, "group": GROUP, "layers": layers,
+            "routing": "softmax top-8 renormalised" + (" + Zipf(1.1) expert bias"
+                                                       if cfg["zipf"] else ""),
+            "parallelism": f"ep{world}" if world > 1 else "single"}
+
+
+def host_info() -> dict:
+    model = None
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    try:
+        import torch
+        tv = torch.__version__
+    except Exception:  # noqa: BLE001
+        tv = None
+    return {"cpu_model": model, "host_threads": os.cpu_count(), "torch": tv,
+            "numpy": np.__version__}
+
+
 # ------------------------------------------------------------------------------------------
 # clocks sampling (nvidia-smi during the timed region)
 # ------------------------------------------------------------------------------------------
@@ -235,29 +269,32 @@ def run_ours(args):
                      (w13, s13, z13, w2, s2, z2), E_total)
     if rank != 0:
         _leave(dist, world)
+    config = base_config(args.workload, world)
+    config.update({
+        "l2": "touched weights > 126 MB L2 (no flush)" if world == 1 else
+              "per-rank weights ~53-105 MB; inputs re-read each step",
+        "rank0_hbm_bytes_per_step": layer_bytes,
+        "layer_hbm_gbs": round(layer_bytes / (ms / 1e3) / 1e9, 1),
+        "layer_hbm_frac_of_measured": round(layer_bytes / (ms / 1e3) / 1e9 / hbm, 4),
+        "layer_tflops": round(flops / (ms / 1e3) / 1e12, 2),
+        "graph": "one CUDA graph per step" if graph is not None else "eager steps"})
     res = {
-        "metric": "MoE-layer tokens/s (Qwen3.6-35B-A3B-shaped, decode T=32)"
-        if args.workload == "decode" else "MoE-layer tokens/s (Qwen3.6-35B-A3B-shaped, prefill T=4096)",
+        "metric": metric_name(args.workload),
         "value": round(tokens_per_s, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 x int4 -> fp32 (fp16 io)",
         "data": "synthetic (seeded; random-init weights of the layer's shapes)",
-        "config": {"workload": f"configs[{1 if args.workload == 'decode' else 2}] MoE layer {args.workload}",
-                   "tokens_per_gpu": T, "hidden": H, "inter": INTER, "experts": E_ROUTED,
-                   "shared_experts": 1, "top_k": TOP_K, "group": GROUP,
-                   "parallelism": f"ep{world}" if world > 1 else "single",
-                   "l2": "touched weights > 126 MB L2 (no flush)" if world == 1 else
-                         "per-rank weights ~53-105 MB; inputs re-read each step",
-                   "rank0_hbm_bytes_per_step": layer_bytes,
-                   "layer_hbm_gbs": round(layer_bytes / (ms / 1e3) / 1e9, 1),
-                   "layer_hbm_frac_of_measured": round(layer_bytes / (ms / 1e3) / 1e9 / hbm, 4),
-                   "layer_tflops": round(flops / (ms / 1e3) / 1e12, 2),
-                   "graph": "one CUDA graph per step" if graph is not None else "eager steps"},
+        "config": config,
         "roofline": dom,
         "clocks": clk.summary(),
         "e2e": e2e,
         "gpu_launches": args.steps * launches_per_step(args.workload, world),
     }
+    if world > 1:
+        res["ep"] = ep_report(torch, dist, world, rank, dev, layer, x, ids, tw, wts, shared)
+    if world == 1 and args.workload == "decode" and not args.no_extras:
+        res["prefill"] = prefill_record(torch, dev, (w13, s13, z13, w2, s2, z2), E_total, args)
+        res["dense"] = dense_record(torch, dev, args)
     if world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(args.workload, budget_s=args.cpu_seconds)
     print(json.dumps(res), flush=True)
@@ -359,6 +396,172 @@ def dominant_kernel(torch, args, world, dist, dev, x, ids, w13, s13, z13, E_tota
                               "capture of the stream kernel)" if world == 1 else None}
 
 
+def _graph_time(torch, fn, steps, warmup):
+    """Capture fn in a CUDA graph (eager if capture fails) and time `steps` replays."""
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            fn()
+    torch.cuda.current_stream().wait_stream(stream)
+    torch.cuda.synchronize()
+    run = fn
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            fn()
+        run = g.replay
+    except Exception:  # noqa: BLE001
+        torch.cuda.synchronize()
+    for _ in range(warmup):
+        run()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(st)
+    for _ in range(steps):
+        run()
+    b.record(st)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps, run is not fn
+
+
+def prefill_record(torch, dev, wts, E_total, args):
+    """configs[2] on the same layer weights: the whole prefill layer (graph replay) and its
+    dominant op (gate_up tile op, tensor-bound), with the clocks seen while it ran."""
+    from w4a8_fp8_wmma.moe_experts import run_grouped_moe
+    import w4a8_fp8_wmma as w4
+    cfg = workload_config("prefill")
+    T = cfg["T"]
+    x_np, ids_np, w_np = make_tokens(T, True, cfg["seed"] * 1000)
+    x = torch.from_numpy(x_np).to(dev)
+    ids = torch.from_numpy(ids_np).to(dev)
+    tw = torch.from_numpy(w_np).to(dev)
+    w13, s13, z13, w2, s2, z2 = wts
+    hbm, fp8_peak, src = peaks()
+
+    def step():
+        run_grouped_moe(x, w13, w2, s13, s2, z13, z2, tw, ids, global_num_experts=E_total,
+                        out_dtype=torch.float16)
+    with ClockSampler(dev.index or 0) as clk:
+        ms, graphed = _graph_time(torch, step, max(5, args.steps // 4), args.warmup)
+        s_, e_, n_ = w4.moe_align_block_size(ids, 128, E_total)
+
+        def op1():
+            torch.ops.w4a8_b200.moe_gemm1_silu(x, w13, s13, z13, s_, e_, n_, ids.size(1), 128,
+                                               6, False)
+        ms1 = _event_time(torch, op1)
+        ident = torch.arange(s_.numel(), dtype=torch.int32, device=dev)
+        buf2 = torch.randn((s_.numel(), INTER), device=dev).half()
+
+        def op2():
+            torch.ops.w4a8_fp8_wmma.mmq_fp8_moe_gemm(buf2, w2, s2, z2, ident, e_, n_, 1, 128,
+                                                     6, False)
+        ms2 = _event_time(torch, op2)
+    rows = int(ids.numel())
+    f1 = 2.0 * rows * 2 * INTER * H
+    f2 = 2.0 * rows * INTER * H
+    layer_flops = f1 + f2
+    return {
+        "workload": "configs[2] MoE layer prefill (T=4096, Zipf-biased top-8 + shared)",
+        "tokens_per_s": round(T / (ms / 1e3), 1), "ms_per_step": round(ms, 4),
+        "graph": graphed,
+        "layer_tflops": round(layer_flops / (ms / 1e3) / 1e12, 1),
+        "layer_frac_of_e4m3_peak": round(layer_flops / (ms / 1e3) / 1e12 / fp8_peak, 4),
+        "roofline": {"kernel": "gate_up tile op (tc_quant_rows_kernel + w4_tc_kernel, SiLU "
+                               "epilogue)", "bound": "tensor",
+                     "achieved": round(f1 / (ms1 / 1e3) / 1e12, 1), "peak": round(fp8_peak, 1),
+                     "unit": "TFLOP/s", "frac": round(f1 / (ms1 / 1e3) / 1e12 / fp8_peak, 4),
+                     "peak_source": f"{src} (e4m3 dense = 2 x measured bf16)",
+                     "algorithmic_flops_per_launch": f1, "avg_launch_us": round(ms1 * 1e3, 2),
+                     "traffic": TC_KERNEL_TRAFFIC},
+        "down_op": {"kernel": "down tile op (tc_quant_rows_kernel + w4_tc_kernel)",
+                    "avg_launch_us": round(ms2 * 1e3, 2),
+                    "tflops": round(f2 / (ms2 / 1e3) / 1e12, 1),
+                    "frac": round(f2 / (ms2 / 1e3) / 1e12 / fp8_peak, 4)},
+        "clocks": clk.summary(),
+    }
+
+
+DENSE_SHAPES = [(2048, 4096), (4096, 2048), (2048, 512), (2048, 8192)]
+
+
+def dense_record(torch, dev, args, Ms=(1, 16, 2048)):
+    """configs[3] dense W4A8 GEMM cells on one GPU: each cell rotates over enough weight copies
+    (>= 256 MB) that every launch reads its weights from HBM, not L2."""
+    import w4a8_fp8_wmma as w4
+    hbm, fp8_peak, src = peaks()
+    g = torch.Generator(device=dev)
+    g.manual_seed(31)
+    cells = []
+    for K, N in DENSE_SHAPES:
+        wbytes = N * K // 2 + N * (K // GROUP) * 2 + (N // 8) * (K // GROUP) * 4
+        copies = max(2, -(-256 * 2 ** 20 // wbytes))
+        ws = [(torch.randint(-2 ** 31, 2 ** 31 - 1, (N, K // 8), dtype=torch.int32, device=dev,
+                             generator=g),
+               (torch.rand((N, K // GROUP), device=dev, generator=g) * 0.019 + 1e-3).half(),
+               torch.randint(-2 ** 31, 2 ** 31 - 1, (N // 8, K // GROUP), dtype=torch.int32,
+                             device=dev, generator=g)) for _ in range(copies)]
+        for M in Ms:
+            x = torch.randn((M, K), device=dev, generator=g).half()
+            kern = 11 if M <= 16 else 10
+            it = [0]
+
+            def launch():
+                w, s, z = ws[it[0] % copies]
+                it[0] += 1
+                torch.ops.w4a8_fp8_wmma.mmq_fp8_gemm(x, w, s, z, kern, False)
+            ms = _event_time(torch, launch, reps=max(copies, 20))
+            byt = wbytes + M * K * 2 + M * N * 2
+            fl = 2.0 * M * N * K
+            cell = {"M": M, "K": K, "N": N, "us": round(ms * 1e3, 2),
+                    "kernel": "decode_gemv (stream)" if kern == 11 else "tile (tcgen05)",
+                    "hbm_gbs": round(byt / (ms / 1e3) / 1e9, 1),
+                    "tflops": round(fl / (ms / 1e3) / 1e12, 2)}
+            if M <= 16:
+                cell.update(bound="hbm", frac=round(byt / (ms / 1e3) / 1e9 / hbm, 4))
+            else:
+                cell.update(bound="tensor", frac=round(fl / (ms / 1e3) / 1e12 / fp8_peak, 4))
+            cells.append(cell)
+        del ws
+        torch.cuda.empty_cache()
+    return {"workload": "configs[3] dense W4A8 sweep (M in {1,16,2048}; weights rotated "
+                        "over >= 256 MB of copies)", "peak_hbm_gbs": hbm,
+            "peak_e4m3_tflops": round(fp8_peak, 1), "peak_source": src, "cells": cells}
+
+
+def ep_report(torch, dist, world, rank, dev, layer, x, ids, tw, wts, shared):
+    """Expert-parallel extras: the all-to-all times of one eager step (CUDA events around each
+    collective, max over ranks) and the output check: every rank all-gathers the per-rank
+    expert weights, runs the single-GPU layer on its own tokens with the full weight set (the
+    shared expert as expert E) and compares it with the EP output (max-abs-rel)."""
+    from w4a8_fp8_wmma.moe_experts import run_grouped_moe
+    layer.profile_a2a = True
+    torch.cuda.synchronize()
+    dist.barrier()
+    y = layer(x, ids[:, :TOP_K].contiguous(), tw[:, :TOP_K].contiguous())
+    torch.cuda.synchronize()
+    layer.profile_a2a = False
+    a2a = [float(_max_over_ranks(torch, dist, world, dev, v)) for v in layer.last_a2a_ms]
+    full = []
+    for t_loc, t_sh in zip(wts, shared):
+        parts = [torch.empty_like(t_loc) for _ in range(world)]
+        dist.all_gather(parts, t_loc.contiguous())
+        full.append(torch.cat(parts + [t_sh], 0).contiguous())
+    w13, s13, z13, w2, s2, z2 = full
+    ref = run_grouped_moe(x, w13, w2, s13, s2, z13, z2, tw, ids,
+                          global_num_experts=E_ROUTED + 1, out_dtype=torch.float32)
+    err = float((y.float() - ref).abs().max() / ref.abs().max().clamp_min(1e-30))
+    err = _max_over_ranks(torch, dist, world, dev, err)
+    del full
+    torch.cuda.empty_cache()
+    return {"a2a_us": [round(v * 1e3, 2) for v in a2a],
+            "a2a_what": list(layer.a2a_names),
+            "parity": {"max_abs_rel": err, "vs": "single-GPU run_grouped_moe with the "
+                       "all-gathered weights on each rank's own tokens (max over ranks)",
+                       "pass": err <= 1e-2}}
+
+
 # dram__bytes_read.sum + dram__bytes_write.sum of the gate_up w4_stream_kernel launch in the
 # committed ncu capture (profiles/w4_stream_kernel_decode.md).
 STREAM_KERNEL_TRAFFIC = 176_702_208 + 6_877_696
@@ -441,18 +644,23 @@ def cpu_layer_sample(workload: str, budget_s: float):
 
 
 def cpu_baseline(workload: str, budget_s: float = 10.0):
+    n = _use_all_threads()
     v, sample = cpu_layer_sample(workload, budget_s)
-    return {"value": round(v, 2), "unit": "tokens/s", "cores": _threads(), "kind": "port",
-            "sample": sample}
+    return {"value": round(v, 2), "unit": "tokens/s", "cores": n, "kind": "port",
+            "sample": sample, "what": "numpy restatement of the reference's torch oracle "
+            "(oracle/w4a8_oracle.py), pinned to fixtures from the reference's own run",
+            **host_info()}
 
 
-def _threads() -> int:
+def _use_all_threads() -> int:
+    """Let the oracle's BLAS use every host thread; returns the thread count set."""
+    n = os.cpu_count() or 1
     try:
         import threadpoolctl
-        info = threadpoolctl.threadpool_info()
-        return int(max((i.get("num_threads", 1) for i in info), default=1))
-    except Exception:
-        return os.cpu_count() or 1
+        threadpoolctl.threadpool_limits(n)
+    except Exception:  # noqa: BLE001
+        pass
+    return n
 
 
 def run_reference(args):
@@ -460,6 +668,7 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    n_threads = _use_all_threads()
     for _ in range(args.warmup):
         cpu_layer_sample(args.workload, 0.0)
     vals = []
@@ -470,19 +679,19 @@ def run_reference(args):
     cfg = workload_config(args.workload)
     res = {
         "impl": "reference",
-        "metric": "MoE-layer tokens/s (Qwen3.6-35B-A3B-shaped, decode T=32)"
-        if args.workload == "decode" else "MoE-layer tokens/s (Qwen3.6-35B-A3B-shaped, prefill T=4096)",
+        "metric": metric_name(args.workload),
         "value": round(v, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "e4m3 x int4 -> fp32 (fp16 io)", "data": "synthetic (seeded)",
-        "config": {"workload": f"configs[{1 if args.workload == 'decode' else 2}] MoE layer {args.workload}",
-                   "tokens_per_gpu": cfg["T"]},
-        "cpu_baseline": {"value": round(v, 2), "unit": "tokens/s", "cores": _threads(),
-                         "kind": "port", "sample": sample},
+        "config": base_config(args.workload, world),
+        "cpu_baseline": {"value": round(v, 2), "unit": "tokens/s", "cores": n_threads,
+                         "kind": "port", "sample": sample, **host_info()},
         "e2e": {"value": round(v, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-        "note": "reference HIP kernels target gfx1201 only; its CPU algorithm (torch oracle) is "
-                "restated in numpy (oracle/w4a8_oracle.py) and timed on the host cores",
+        "note": "the reference's kernels are gfx1201 HIP and cannot run here; its CPU algorithm "
+                "(the torch oracle of its tests) is restated in numpy (oracle/w4a8_oracle.py, "
+                "a port pinned to fixtures from the reference's own run) and timed on the "
+                "host cores",
     }
     print(json.dumps(res))
 
@@ -517,6 +726,8 @@ def main():
     ap.add_argument("--workload", choices=["decode", "prefill"], default="decode")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the prefill and dense sub-records of the default run")
     ap.add_argument("--profile-op", action="store_true",
                     help="only launch the gate_up op --steps times (for an ncu capture)")
     args = ap.parse_args()

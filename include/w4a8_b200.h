@@ -100,8 +100,11 @@ W4A8_API int w4a8_moe_align_block_size(const int32_t* topk_ids, int64_t num_slot
  * comes from vLLM. The per-expert offsets live in a fixed 16 KB device array inside the
  * library, so num_local_experts is limited to 4095 (larger values return W4A8_ERR_INVALID).
  * The first call on each device looks the array's address up (cudaGetSymbolAddress) with that
- * device current; make that first call before any stream capture. The array is shared by all
- * calls on a device: calls that overlap on the GPU (different streams, no ordering) race.
+ * device current; make that first call before any stream capture. The address is cached for the
+ * life of the process, which assumes the device's primary context lives as long (no
+ * cudaDeviceReset between calls). A failed lookup returns W4A8_ERR_INVALID with the CUDA error
+ * in w4a8_last_error(). The array is shared by all calls on a device: calls that overlap on the
+ * GPU (different streams, no ordering) race.
  * Arguments and results are those of w4a8_moe_align_block_size.
  */
 W4A8_API int w4a8_moe_align_block_size_noalloc(const int32_t* topk_ids, int64_t num_slots,

@@ -285,13 +285,18 @@ int noalloc_scratch(void** out) {
     static void* addr[kMaxDevices] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return (int)e;
+    if (e != cudaSuccess)
+        return w4a8::set_error(std::string("moe_align_noalloc: cudaGetDevice failed: ") +
+                               cudaGetErrorString(e));
     if (dev < 0 || dev >= kMaxDevices) return w4a8::set_error("moe_align_noalloc: device index out of range");
     std::lock_guard<std::mutex> lock(mu);
     if (!addr[dev]) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_align_noalloc_scratch);
-        if (e != cudaSuccess) return (int)e;
+        if (e != cudaSuccess)
+            return w4a8::set_error(
+                std::string("moe_align_noalloc: cudaGetSymbolAddress failed: ") +
+                cudaGetErrorString(e));
         addr[dev] = p;
     }
     *out = addr[dev];

@@ -78,6 +78,12 @@ class ExpertParallelMoE:
                     cat.append(torch.cat([t_r, t_s], 0).contiguous())
             self.w_all = tuple(cat)
         self._ntp = {}  # cached device scalars (no host->device copies inside graph capture)
+        # profile_a2a: record CUDA events around each collective of the next eager step and
+        # leave their durations (ms) in last_a2a_ms, in the order of a2a_names
+        self.profile_a2a = False
+        self.last_a2a_ms: list[float] = []
+        self.a2a_names = ("dispatch rows", "dispatch ids", "combine rows")
+        self._ev = []
 
     # ---- compute on received rows ------------------------------------------------------
     def _gpu_experts(self, rows: torch.Tensor, local_ids: torch.Tensor) -> torch.Tensor:
@@ -152,8 +158,8 @@ class ExpertParallelMoE:
             x.contiguous(), topk_ids.to(torch.int32).contiguous(), self.E_loc, W, C)
         recv_x = torch.empty_like(send_x)
         recv_id = torch.empty_like(send_id)
-        dist.all_to_all_single(recv_x, send_x, group=self.group)
-        dist.all_to_all_single(recv_id, send_id, group=self.group)
+        self._a2a(recv_x, send_x)
+        self._a2a(recv_id, send_id)
         self.last_recv = (recv_x, recv_id)  # for profiling tools: this step's received rows
         sh = None
         if self._fused_shared:
@@ -169,9 +175,23 @@ class ExpertParallelMoE:
             y = self.expert_fn(recv_x, recv_id).to(x.dtype).contiguous()  # (W*C, H)
             sh = self._shared(x)
         back = torch.empty_like(y)
-        dist.all_to_all_single(back, y, group=self.group)
+        self._a2a(back, y)
+        if self.profile_a2a:
+            torch.cuda.synchronize()
+            self.last_a2a_ms = [a.elapsed_time(b) for a, b in self._ev]
+            self._ev = []
         tw = topk_weights.reshape(-1).to(torch.float32).contiguous()
         return torch.ops.w4a8_b200.ep_combine(back, slot_row, tw,
                                               None if sh is None else sh.contiguous(), k)
+
+    def _a2a(self, out, inp):
+        if not self.profile_a2a:
+            dist.all_to_all_single(out, inp, group=self.group)
+            return
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        dist.all_to_all_single(out, inp, group=self.group)
+        b.record()
+        self._ev.append((a, b))
 
     __call__ = forward

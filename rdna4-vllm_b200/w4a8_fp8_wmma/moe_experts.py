@@ -176,3 +176,29 @@ def wna16_moe_to_op_layout(qweight_u8: torch.Tensor, scales: torch.Tensor,
         z = (zi[:, :, 0] | (zi[:, :, 1] << 8) | (zi[:, :, 2] << 16) | (zi[:, :, 3] << 24))
         z = z.contiguous()
     return w, s, z
+
+
+def mxfp4_to_op_layout(weight_packed: torch.Tensor, weight_scale: torch.Tensor):
+    """OCP mxfp4 (E2M1 codes + E8M0 block exponents) -> op layout, for weight_is_e2m1=True.
+
+    weight_packed (..., N, K/2) uint8, two E2M1 codes per byte with the lower K index in the low
+    nibble; weight_scale (..., N, K/32) uint8 E8M0 (value 2^(s-127)). Returns w (..., N, K/8)
+    int32 holding the codes unchanged (code j of a word = input channel 8w + j) and fp16 group
+    scales 2^(s-127) (group_size 32), the reference's mxfp4/convert.py:convert_mxfp4_moe
+    contract. There are no zero points (E2M1 is symmetric). Scales outside fp16's range are
+    rejected instead of saturating: the kernels carry fp16 group scales."""
+    if weight_packed.dtype != torch.uint8 or weight_scale.dtype != torch.uint8:
+        raise TypeError("mxfp4 weight_packed and weight_scale must be uint8")
+    K = weight_packed.size(-1) * 2
+    if K % 32 or weight_scale.size(-1) != K // 32:
+        raise ValueError(f"mxfp4 needs K % 32 == 0 and K/32 scale blocks; got K={K}, "
+                         f"{weight_scale.size(-1)} blocks")
+    if bool((weight_scale == 0xFF).any()):
+        raise ValueError("mxfp4 scale holds the E8M0 NaN code 0xFF")
+    exp = weight_scale.to(torch.int32) - 127
+    if bool((exp > 15).any()):
+        raise ValueError("mxfp4 block scale above 2^15 does not fit the fp16 group scales")
+    # two codes per byte, K-packed: four consecutive bytes are one little-endian int32 word
+    w = weight_packed.contiguous().view(torch.int32)
+    s = torch.ldexp(torch.ones_like(exp, dtype=torch.float32), exp).to(torch.float16)
+    return w, s

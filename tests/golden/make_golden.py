@@ -158,7 +158,57 @@ def main(ref_root: str) -> None:
     conv["silu_in"] = o1
     conv["silu_out"] = te.silu_and_mul_ref(t(o1)).numpy()
     np.savez_compressed(os.path.join(HERE, "convert.npz"), **conv)
+    formats(ref_root)
     print("fixtures written to", HERE)
+
+
+def formats(ref_root: str) -> None:
+    """compressed-tensors GPTQ, MoeWNA16 and mxfp4 checkpoints -> op layout, through the
+    reference's own converters (moe_experts.py:437 _ct_moe_to_op_layout, :473
+    _wna16_moe_to_op_layout; mxfp4/convert.py convert_mxfp4_moe / convert_mxfp4_weight), plus
+    the reference's mxfp4 dense oracle (mxfp4/test_mxfp4_kernel_gpu.py:64-71) run on CPU."""
+    if "w4a8_fp8_wmma" not in sys.modules:
+        load_reference(ref_root)
+    from w4a8_fp8_wmma.moe_experts import _ct_moe_to_op_layout, _wna16_moe_to_op_layout
+    spec = importlib.util.spec_from_file_location(
+        "ref_mxfp4_convert", os.path.join(ref_root, "w4a8_fp8_wmma", "mxfp4", "convert.py"))
+    mx = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mx)
+    out = {}
+    rng = np.random.default_rng(51)
+    # compressed-tensors: (E, K/8, N) int32 natural nibble order along K, scales (E, K/g, N)
+    E, K, N, g = 3, 256, 64, 32
+    ct_q = rng.integers(-2 ** 31, 2 ** 31 - 1, (E, K // 8, N), dtype=np.int64).astype(np.int32)
+    ct_s = rng.uniform(1e-3, 2e-2, (E, K // g, N)).astype(np.float16)
+    w, s = _ct_moe_to_op_layout(t(ct_q), t(ct_s))
+    out.update(ct_qweight=ct_q, ct_scales=ct_s, ct_op_w=w.numpy(), ct_op_s=s.numpy())
+    # MoeWNA16: qweight (E, N, K/2) u8, scales (E, N, K/g), qzeros (E, N/2, K/g) u8
+    wq = rng.integers(0, 256, (E, N, K // 2), dtype=np.int64).astype(np.uint8)
+    ws = rng.uniform(1e-3, 2e-2, (E, N, K // g)).astype(np.float16)
+    wz = rng.integers(0, 256, (E, N // 2, K // g), dtype=np.int64).astype(np.uint8)
+    w, s, z = _wna16_moe_to_op_layout(t(wq), t(ws), t(wz))
+    out.update(wna16_qweight=wq, wna16_scales=ws, wna16_qzeros=wz, wna16_op_w=w.numpy(),
+               wna16_op_s=s.numpy(), wna16_op_z=z.numpy())
+    # mxfp4: weight_packed (E, N, K/2) u8 E2M1 pairs, weight_scale (E, N, K/32) u8 E8M0
+    mp = rng.integers(0, 256, (E, N, K // 2), dtype=np.int64).astype(np.uint8)
+    ms = rng.integers(124, 131, (E, N, K // 32), dtype=np.int64).astype(np.uint8)
+    conv = mx.convert_mxfp4_moe(t(mp), t(ms))
+    out.update(mx_packed=mp, mx_scale=ms, mx_op_w=conv["w_packed"].numpy(),
+               mx_op_s=conv["scales"].numpy())
+    # the reference's mxfp4 dense oracle on one expert (reciprocal-multiply act quant)
+    x = (rng.standard_normal((16, K), dtype=np.float32) * 0.5).astype(np.float16)
+    c1 = mx.convert_mxfp4_weight(t(mp[0]), t(ms[0]))
+    spec2 = importlib.util.spec_from_file_location(
+        "ref_mxfp4_gpu_test",
+        os.path.join(ref_root, "w4a8_fp8_wmma", "mxfp4", "test_mxfp4_kernel_gpu.py"))
+    src = open(spec2.origin).read()
+    fn_src = src[src.index("def fp8_dense_ref"):src.index("def run_oracle")]
+    ns = {"torch": torch, "unpack_e2m1_nibbles": mx.unpack_e2m1_nibbles,
+          "FP4_E2M1_LUT": mx.FP4_E2M1_LUT, "OCP_MX_BLOCK_SIZE": mx.OCP_MX_BLOCK_SIZE}
+    exec(compile(fn_src, spec2.origin, "exec"), ns)  # the function alone (the module needs a GPU)
+    ref = ns["fp8_dense_ref"](t(x), t(mp[0]), t(ms[0]), c1)
+    out.update(mx_x=x, mx_dense_ref=ref.numpy())
+    np.savez_compressed(os.path.join(HERE, "formats.npz"), **out)
 
 
 def tc_pack(codes):
@@ -173,4 +223,8 @@ def tc_pack(codes):
 if __name__ == "__main__":
     if len(sys.argv) < 2:
         sys.exit("usage: python tests/golden/make_golden.py <path to the reference checkout>")
-    main(sys.argv[1])
+    if len(sys.argv) > 2 and sys.argv[2] == "--formats-only":
+        torch.manual_seed(0)
+        formats(sys.argv[1])
+    else:
+        main(sys.argv[1])
