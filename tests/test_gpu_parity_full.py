@@ -84,6 +84,18 @@ def check_layer(x, wts, ids, w, kernel="wmma"):
     return err
 
 
+def test_torch_ref_act_quant_bit_exact_on_gpu(w4):
+    """The reference's quantisation must be the oracle's on the GPU too (bytes and scales)."""
+    rng = np.random.default_rng(90)
+    x = (rng.standard_normal((512, 2048), dtype=np.float32) * 3).astype(np.float16)
+    q, s = R.act_quant(cu(x))
+    qr, sr = O.act_quant(x)
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), sr.view(np.uint32))
+    assert np.array_equal(q.cpu().numpy().view(np.uint32), O.e4m3_decode(qr).view(np.uint32))
+    qk, sk = w4.act_quant_fp8(cu(x))
+    assert np.array_equal(qk.cpu().numpy(), qr)
+
+
 # ------------------------------------------------------------ configs[2] and the tile path ---
 def test_layer_configs2_prefill_zipf(w4):
     wts = rand_layer(2000, 257)
@@ -115,20 +127,20 @@ def test_layer_decode_configs1(w4):
 
 
 # ------------------------------------------------------------ adversarial activations --------
-def adversarial(kind, T, K, seed):
+def adversarial(kind, T, K, seed, outlier=60000.0, const=3.0):
     rng = np.random.default_rng(seed)
     base = rng.standard_normal((T, K), dtype=np.float32)
     if kind == "positive":
         x = np.abs(base) + 0.5
     elif kind == "outlier":
         x = base.copy()
-        x[:, 17] = 60000.0
-        x[::2, 1000 % K] = -60000.0
+        x[:, 17] = outlier
+        x[::2, 1000 % K] = -outlier
     elif kind == "post_silu":
         g = base * 3.0
         x = g / (1.0 + np.exp(-g))
     elif kind == "constant":
-        x = np.full((T, K), 3.0, np.float32)
+        x = np.full((T, K), const, np.float32)
     else:
         raise ValueError(kind)
     return x.astype(np.float16)
@@ -167,10 +179,15 @@ def test_grouped_gemv_adversarial(w4, kind):
 
 @pytest.mark.parametrize("kind", KINDS)
 def test_fused_decode_layer_adversarial(w4, kind):
+    """The whole decode layer (M <= 96: the fused decode op). Outliers of 200 sigma and
+    constant rows of 0.05 keep the fp16 intermediates finite: at 60000 the reference's own
+    fp16 gate/up product overflows to inf (the single-GEMM tests above cover 60000)."""
     wts = rand_layer(2400, 257)
     _, ids, w = tokens(3, 32, 256, 8, zipf=False)
-    x = adversarial(kind, 32, H, 62)
-    check_layer(x, wts, ids, w, kernel="wmma")  # M <= 96: the fused decode op
+    x = adversarial(kind, 32, H, 62, outlier=200.0, const=0.05)
+    xd, idd, wd = cu(x), cu(ids), cu(w)
+    assert torch.isfinite(R.moe_layer(xd, *wts, idd, wd)).all()
+    check_layer(x, wts, ids, w, kernel="wmma")
 
 
 # ------------------------------------------------------------ mxfp4 (E2M1) -----------------

@@ -2,8 +2,8 @@
 finish in seconds (configs[2]: 4096 tokens x 257 experts). TEST INFRASTRUCTURE ONLY.
 
 It restates oracle/w4a8_oracle.py:moe_layer with torch tensors on any device:
-  * activation quant — fp32 IEEE divide, then torch's float8_e4m3fn conversion (the reference
-    oracle's own op, w4a8_fp8_wmma/test_correctness.py:74-76);
+  * activation quant — fp32 IEEE divides (tensor by tensor), then torch's float8_e4m3fn
+    conversion (the reference oracle's own op, w4a8_fp8_wmma/test_correctness.py:74-76);
   * each GEMM — dequantised weights scale*(q - z) in fp32 times the e4m3 activations, then the
     activation scale, rounded to fp16 (the oracle sums per 128-group first; the two associations
     differ by fp32 rounding only);
@@ -47,7 +47,9 @@ def dequant(w: torch.Tensor, s: torch.Tensor, z: torch.Tensor | None) -> torch.T
 def act_quant(x: torch.Tensor):
     xf = x.float()
     amax = xf.abs().amax(dim=1).clamp(min=1e-8 * 448.0)
-    scale = amax / 448.0
+    # tensor / tensor: torch's CUDA divide by a Python scalar multiplies by the reciprocal,
+    # which is not the oracle's IEEE divide
+    scale = amax / torch.full_like(amax, 448.0)
     q = (xf / scale[:, None]).to(torch.float8_e4m3fn).float()
     return q, scale
 
