@@ -245,6 +245,34 @@ W4A8_API int w4a8_moe_decode(const void* x, const int32_t* topk_ids, const float
                              int64_t group_size, void* out, void* workspace,
                              size_t workspace_bytes, w4a8_stream_t stream);
 
+/*
+ * Load-time weight prepack for the decode GEMV (no counterpart kernel in the reference; it is
+ * the device-side analogue of the reference's load-time layout converters,
+ * w4a8_fp8_wmma/w4a8_fp8_wmma/moe_experts.py:331-482). One GEMM operand (w13 with
+ * gate_up = 1, or w2 with gate_up = 0) in the op layout above becomes one contiguous
+ * 34,048-byte block per (expert, 128-row slice, 512-wide K chunk): the slice's codes in the
+ * GEMV's swizzled shared-memory order, then its fp16 scales and packed zero points (8 when
+ * w_zeros is NULL). A gate_up slice holds gate rows [64s, 64s+64) and the matching up rows.
+ * Needs K % 512 == 0, N % 128 == 0. Size: w4a8_stream_pack_size.
+ */
+W4A8_API size_t w4a8_stream_pack_size(int64_t E, int64_t N, int64_t K);
+W4A8_API int w4a8_stream_pack(const int32_t* w_packed, const void* scales, const int32_t* w_zeros,
+                              int64_t E, int64_t N, int64_t K, int32_t gate_up, void* packed,
+                              size_t packed_bytes, w4a8_stream_t stream);
+
+/*
+ * w4a8_moe_decode on prepacked weights (p13 from w4a8_stream_pack(w13, gate_up = 1), p2 from
+ * w4a8_stream_pack(w2, gate_up = 0)): the same arithmetic and result, in three launches
+ * (routing sort + token quantisation; gate_up GEMV with SiLU; down GEMV with the slot-order
+ * reduce). Needs hidden and inter multiples of 512, top_k <= 16, T*top_k <= 65536,
+ * E <= 4096. Workspace: w4a8_moe_decode_workspace_size.
+ */
+W4A8_API int w4a8_moe_decode_packed(const void* x, const int32_t* topk_ids,
+                                    const float* topk_weights, int64_t T, int64_t top_k,
+                                    int64_t E, const void* p13, const void* p2, int64_t H,
+                                    int64_t I, void* out, void* workspace,
+                                    size_t workspace_bytes, w4a8_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -24,7 +24,7 @@ OBJ = os.path.join(HERE, "_build")
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 
-CU_SOURCES = ["act_quant.cu", "moe_align.cu", "gemm_mma.cu", "gemv_stream.cu", "gemm_tc.cu", "reduce.cu", "moe_layer.cu", "ep_dispatch.cu",
+CU_SOURCES = ["act_quant.cu", "moe_align.cu", "gemm_mma.cu", "gemv_stream.cu", "gemm_tc.cu", "reduce.cu", "moe_layer.cu", "moe_decode.cu", "ep_dispatch.cu",
               "capi.cu"]
 LIB = os.path.join(PKG, "libw4a8_b200.so")
 SHIM = os.path.join(PKG, "_C.so")

@@ -24,4 +24,16 @@ int launch_gather_reduce(const __half* out2, const int32_t* slot_to_row, const f
                          void* out, bool out_half, int64_t M, int64_t N, int top_k,
                          cudaStream_t stream);
 
+// Fused decode layer (moe_decode.cu): three launches, see there.
+bool fused_decode_ok(int64_t T, int64_t top_k, int64_t E, int64_t H, int64_t I);
+size_t fused_decode_workspace(int64_t T, int64_t top_k, int64_t E, int64_t H, int64_t I);
+int launch_fused_decode(const void* x, const int32_t* topk_ids, const float* topk_weights,
+                        int64_t T, int64_t top_k, int64_t E, const int32_t* w13, const void* s13,
+                        const int32_t* z13, const int32_t* w2, const void* s2, const int32_t* z2,
+                        int64_t H, int64_t I, void* out, void* workspace, cudaStream_t st,
+                        const void* p13 = nullptr, const void* p2 = nullptr);
+size_t stream_pack_bytes(int64_t E, int64_t N, int64_t K);
+int launch_stream_pack(const int32_t* w, const void* scales, const int32_t* zeros, int64_t E,
+                       int64_t N, int64_t K, int gate_up, void* packed, cudaStream_t st);
+
 }  // namespace w4a8

@@ -11,6 +11,7 @@
 //   7. gather-reduce in slot order -> (T, H) fp16 output
 // The down output is rounded to fp16 per (token, slot) before the weighted sum, the
 // association of the reference oracle (w4a8_fp8_wmma/test_moe_experts.py:182-190).
+#include <algorithm>
 #include <string>
 
 #include "common.cuh"
@@ -63,7 +64,9 @@ using namespace w4a8;
 extern "C" size_t w4a8_moe_decode_workspace_size(int64_t T, int64_t top_k, int64_t E, int64_t H,
                                                  int64_t I) {
     if (T < 0 || top_k <= 0 || E <= 0 || H <= 0 || I <= 0) return 0;
-    return decode_layout(T, top_k, E, H, I).total;
+    size_t b = decode_layout(T, top_k, E, H, I).total;
+    if (fused_decode_ok(T, top_k, E, H, I)) b = std::max(b, fused_decode_workspace(T, top_k, E, H, I));
+    return b;
 }
 
 extern "C" int w4a8_moe_decode(const void* x, const int32_t* topk_ids, const float* topk_weights,
@@ -83,9 +86,15 @@ extern "C" int w4a8_moe_decode(const void* x, const int32_t* topk_ids, const flo
         return set_error(o + ": null pointer");
     if (!stream_path_ok(H, (int)(H / 128), 0, w13) || !stream_path_ok(I, (int)(I / 128), 0, w2))
         return set_error(o + ": weights must be 16-byte aligned");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (fused_decode_ok(T, top_k, E, H, I)) {
+        if (!workspace || workspace_bytes < fused_decode_workspace(T, top_k, E, H, I))
+            return set_error(o + ": workspace too small");
+        return launch_fused_decode(x, topk_ids, topk_weights, T, top_k, E, w13, s13, z13, w2, s2,
+                                   z2, H, I, out, workspace, st);
+    }
     const DecodeLayout L = decode_layout(T, top_k, E, H, I);
     if (!workspace || workspace_bytes < L.total) return set_error(o + ": workspace too small");
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     int32_t* sorted = reinterpret_cast<int32_t*>(ws + L.off_sorted);
     int32_t* eids = reinterpret_cast<int32_t*>(ws + L.off_eids);
@@ -163,4 +172,47 @@ extern "C" int w4a8_moe_decode(const void* x, const int32_t* topk_ids, const flo
     if (int rc = launch_w4_stream(g2, st)) return rc;
     // 7. topk-weighted gather-reduce in slot order -> fp16
     return launch_gather_reduce(out2, map, topk_weights, out, true, T, H, (int)top_k, st);
+}
+
+extern "C" size_t w4a8_stream_pack_size(int64_t E, int64_t N, int64_t K) {
+    if (E <= 0 || N <= 0 || K <= 0 || N % 128 != 0 || K % 512 != 0) return 0;
+    return stream_pack_bytes(E, N, K);
+}
+
+extern "C" int w4a8_stream_pack(const int32_t* w_packed, const void* scales, const int32_t* w_zeros,
+                                int64_t E, int64_t N, int64_t K, int32_t gate_up, void* packed,
+                                size_t packed_bytes, w4a8_stream_t stream) {
+    const std::string o = "stream_pack";
+    if (E <= 0 || N <= 0 || K <= 0) return set_error(o + ": bad sizes");
+    if (K % 512 != 0 || N % 128 != 0 || (gate_up && (N / 2) % 64 != 0))
+        return set_error(o + ": needs K % 512 == 0 and N % 128 == 0");
+    if (!w_packed || !scales || !packed) return set_error(o + ": null pointer");
+    if ((reinterpret_cast<uintptr_t>(w_packed) & 15) || (reinterpret_cast<uintptr_t>(packed) & 15) ||
+        (reinterpret_cast<uintptr_t>(scales) & 7) || (w_zeros && (reinterpret_cast<uintptr_t>(w_zeros) & 15)))
+        return set_error(o + ": weights, zeros and the output must be 16-byte aligned");
+    if (packed_bytes < stream_pack_bytes(E, N, K)) return set_error(o + ": output too small");
+    return launch_stream_pack(w_packed, scales, w_zeros, E, N, K, gate_up ? 1 : 0, packed,
+                              reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int w4a8_moe_decode_packed(const void* x, const int32_t* topk_ids,
+                                      const float* topk_weights, int64_t T, int64_t top_k,
+                                      int64_t E, const void* p13, const void* p2, int64_t H,
+                                      int64_t I, void* out, void* workspace,
+                                      size_t workspace_bytes, w4a8_stream_t stream) {
+    const std::string o = "moe_decode_packed";
+    if (T < 0 || top_k <= 0 || E <= 0 || H <= 0 || I <= 0) return set_error(o + ": bad sizes");
+    if (!fused_decode_ok(T, top_k, E, H, I))
+        return set_error(o + ": needs hidden, inter % 512 == 0, top_k <= 16, T*top_k <= 65536, "
+                             "E <= 4096");
+    if (T == 0) return W4A8_OK;
+    if (!x || !topk_ids || !topk_weights || !p13 || !p2 || !out) return set_error(o + ": null pointer");
+    if ((reinterpret_cast<uintptr_t>(p13) & 15) || (reinterpret_cast<uintptr_t>(p2) & 15) ||
+        (reinterpret_cast<uintptr_t>(x) & 15))
+        return set_error(o + ": x and the packed weights must be 16-byte aligned");
+    if (!workspace || workspace_bytes < fused_decode_workspace(T, top_k, E, H, I))
+        return set_error(o + ": workspace too small");
+    return launch_fused_decode(x, topk_ids, topk_weights, T, top_k, E, nullptr, nullptr, nullptr,
+                               nullptr, nullptr, nullptr, H, I, out, workspace,
+                               reinterpret_cast<cudaStream_t>(stream), p13, p2);
 }

@@ -357,6 +357,53 @@ at::Tensor ep_combine_forward(const at::Tensor& back, const at::Tensor& slot_row
     return out;
 }
 
+at::Tensor stream_pack_forward(const at::Tensor& w, const at::Tensor& s, const at::Tensor& z,
+                               bool gate_up) {
+    TORCH_CHECK(w.is_cuda() && w.dim() == 3 && w.scalar_type() == at::kInt && w.is_contiguous(),
+                "w must be a contiguous (E, N, K/8) int32 CUDA tensor");
+    TORCH_CHECK(s.scalar_type() == at::kHalf && s.is_contiguous(), "scales must be contiguous fp16");
+    const int64_t E = w.size(0), N = w.size(1), K = w.size(2) * 8;
+    TORCH_CHECK(s.numel() == E * N * (K / 128), "scales must be (E, N, K/128)");
+    const bool zz = z.defined() && z.numel() > 0;
+    if (zz)
+        TORCH_CHECK(z.scalar_type() == at::kInt && z.is_contiguous() && z.numel() == E * (N / 8) * (K / 128),
+                    "zeros must be (E, N/8, K/128) int32");
+    const c10::cuda::CUDAGuard guard(w.device());
+    const size_t bytes = w4a8_stream_pack_size(E, N, K);
+    TORCH_CHECK(bytes > 0, "stream_pack: needs K % 512 == 0 and N % 128 == 0");
+    auto out = at::empty({(int64_t)bytes}, w.options().dtype(at::kByte));
+    check_status(w4a8_stream_pack(w.data_ptr<int32_t>(), s.data_ptr(), zz ? z.data_ptr<int32_t>() : nullptr,
+                                  E, N, K, gate_up ? 1 : 0, out.data_ptr(), bytes, cur_stream()),
+                 "stream_pack");
+    return out;
+}
+
+at::Tensor moe_decode_packed_forward(const at::Tensor& x, const at::Tensor& p13,
+                                     const at::Tensor& p2, int64_t E, int64_t I,
+                                     const at::Tensor& topk_weights, const at::Tensor& topk_ids) {
+    TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kHalf && x.dim() == 2 && x.is_contiguous(),
+                "x must be a contiguous (T, H) fp16 CUDA tensor");
+    TORCH_CHECK(topk_ids.scalar_type() == at::kInt && topk_weights.scalar_type() == at::kFloat &&
+                    topk_ids.is_contiguous() && topk_weights.is_contiguous() &&
+                    topk_ids.dim() == 2 && topk_weights.sizes() == topk_ids.sizes() &&
+                    topk_ids.size(0) == x.size(0),
+                "topk_ids (T, k) int32 and topk_weights (T, k) fp32 must be contiguous");
+    const int64_t T = x.size(0), H = x.size(1), k = topk_ids.size(1);
+    TORCH_CHECK(p13.scalar_type() == at::kByte && p2.scalar_type() == at::kByte &&
+                    (size_t)p13.numel() == w4a8_stream_pack_size(E, 2 * I, H) &&
+                    (size_t)p2.numel() == w4a8_stream_pack_size(E, H, I),
+                "p13 / p2 must be stream_pack outputs for (E, 2*inter, hidden) / (E, hidden, inter)");
+    const c10::cuda::CUDAGuard guard(x.device());
+    auto out = at::empty({T, H}, x.options());
+    auto ws = workspace(x, w4a8_moe_decode_workspace_size(T, k, E, H, I));
+    check_status(w4a8_moe_decode_packed(x.data_ptr(), topk_ids.data_ptr<int32_t>(),
+                                        topk_weights.data_ptr<float>(), T, k, E, p13.data_ptr(),
+                                        p2.data_ptr(), H, I, out.data_ptr(), ws.data_ptr(),
+                                        (size_t)ws.numel(), cur_stream()),
+                 "moe_decode_packed");
+    return out;
+}
+
 at::Tensor moe_decode_forward(const at::Tensor& x, const at::Tensor& w13, const at::Tensor& s13,
                               const at::Tensor& z13, const at::Tensor& w2, const at::Tensor& s2,
                               const at::Tensor& z2, const at::Tensor& topk_weights,
@@ -447,6 +494,9 @@ TORCH_LIBRARY(w4a8_b200, m) {
     m.def("ep_dispatch(Tensor x, Tensor topk_ids, int experts_per_rank, int world, int capacity) -> Tensor[]");
     m.def("ep_combine(Tensor back, Tensor slot_row, Tensor topk_weights, Tensor? shared, int top_k) -> Tensor");
     // Whole gated MoE layer at decode sizes (align -> gate_up+SiLU -> down -> reduce).
+    m.def("stream_pack(Tensor w, Tensor scales, Tensor zeros, bool gate_up) -> Tensor");
+    m.def("moe_decode_packed(Tensor x, Tensor p13, Tensor p2, int num_experts, int inter, "
+          "Tensor topk_weights, Tensor topk_ids) -> Tensor");
     m.def("moe_decode(Tensor x, Tensor w13, Tensor s13, Tensor z13, Tensor w2, Tensor s2, "
           "Tensor z2, Tensor topk_weights, Tensor topk_ids) -> Tensor");
     // Fused gate_up + SiLU with any MoE kernel id (0 scalar, 6 tile, 7 GEMV).
@@ -463,6 +513,8 @@ TORCH_LIBRARY_IMPL(w4a8_b200, CUDA, m) {
     m.impl("ep_dispatch", &ep_dispatch_forward);
     m.impl("ep_combine", &ep_combine_forward);
     m.impl("moe_decode", &moe_decode_forward);
+    m.impl("stream_pack", &stream_pack_forward);
+    m.impl("moe_decode_packed", &moe_decode_packed_forward);
     m.impl("moe_gemm1_silu", &gemm1_silu_impl);
     m.impl("moe_align_block_size", &moe_align_block_size_forward);
 }

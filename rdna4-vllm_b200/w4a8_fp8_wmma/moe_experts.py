@@ -14,6 +14,7 @@ AWQ (moe_experts.py:331-396), compressed-tensors GPTQ (:409-454), MoeWNA16 (:473
 from __future__ import annotations
 
 import os
+import weakref
 
 import torch
 
@@ -67,12 +68,9 @@ def run_grouped_moe(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, w1_s: t
     use_gemv = kernel != "scalar" and M <= GEMV_MAX_M
     if (use_gemv and expert_map is None and not apply_router_weight_on_input
             and _fused_decode_ok(x, w1, w2, w1_s, w2_s, w1_zp, w2_zp, E_global)):
-        # whole layer in one op: align -> gate_up+SiLU -> down -> reduce (7 launches)
-        z1 = w1_zp if w1_zp is not None else torch.empty(0, dtype=torch.int32, device=dev)
-        z2 = w2_zp if w2_zp is not None else torch.empty(0, dtype=torch.int32, device=dev)
-        y = torch.ops.w4a8_b200.moe_decode(
-            x.contiguous(), w1, w1_s.contiguous(), z1, w2, w2_s.contiguous(), z2,
-            topk_weights.to(torch.float32).contiguous(), topk_ids.to(torch.int32).contiguous())
+        # whole layer on the prepacked weights: routing sort + token quant -> gate_up+SiLU ->
+        # down + slot-order reduce (3 launches)
+        y = decode_pack_for(w1, w2, w1_s, w2_s, w1_zp, w2_zp)(x, topk_weights, topk_ids)
         return y if out_dtype == torch.float16 else y.to(out_dtype)
     block_m = GEMV_BLOCK_M if use_gemv else TILE_BLOCK_M
     gver = "gemv" if use_gemv else kernel
@@ -100,6 +98,49 @@ def run_grouped_moe(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, w1_s: t
                             w_zeros=w2_zp)
     acc = mmq_fp8_moe_gather_reduce(out2, sorted_ids, tw, ntp, top_k)
     return acc.to(out_dtype)
+
+
+class DecodePack:
+    """One MoE layer's weights prepacked for the decode path (a load-time step, like the
+    reference's layout converters): w13 and w2 as contiguous GEMV stage blocks with their
+    scales and zero points (torch.ops.w4a8_b200.stream_pack). The op-layout tensors stay the
+    source of truth; the pack is derived from them."""
+
+    def __init__(self, w1, w2, w1_s, w2_s, w1_zp=None, w2_zp=None):
+        dev = w1.device
+        z1 = w1_zp if w1_zp is not None else torch.empty(0, dtype=torch.int32, device=dev)
+        z2 = w2_zp if w2_zp is not None else torch.empty(0, dtype=torch.int32, device=dev)
+        self.E = w1.size(0)
+        self.inter = w1.size(1) // 2
+        self.hidden = w1.size(2) * 8
+        self.p13 = torch.ops.w4a8_b200.stream_pack(w1, w1_s.contiguous(), z1, True)
+        self.p2 = torch.ops.w4a8_b200.stream_pack(w2, w2_s.contiguous(), z2, False)
+
+    def __call__(self, x, topk_weights, topk_ids):
+        return torch.ops.w4a8_b200.moe_decode_packed(
+            x.contiguous(), self.p13, self.p2, self.E, self.inter,
+            topk_weights.to(torch.float32).contiguous(), topk_ids.to(torch.int32).contiguous())
+
+
+# Packs built on first use, keyed by the identity (and version) of the op-layout tensors; the
+# entry dies with them. A caller that manages its own load step can build DecodePack directly.
+_PACKS: dict[int, tuple] = {}
+
+
+def decode_pack_for(w1, w2, w1_s, w2_s, w1_zp, w2_zp) -> DecodePack:
+    key = id(w1)
+    srcs = (w1, w2, w1_s, w2_s, w1_zp, w2_zp)
+    ent = _PACKS.get(key)
+    if ent is not None:
+        refs, vers, pack = ent
+        if all((r() is t) if t is not None else r is None for r, t in zip(refs, srcs)) and \
+                vers == tuple(t._version if t is not None else 0 for t in srcs):
+            return pack
+    pack = DecodePack(*srcs)
+    refs = tuple(weakref.ref(t) if t is not None else None for t in srcs)
+    _PACKS[key] = (refs, tuple(t._version if t is not None else 0 for t in srcs), pack)
+    weakref.finalize(w1, _PACKS.pop, key, None)
+    return pack
 
 
 def _fused_decode_ok(x, w1, w2, w1_s, w2_s, w1_zp, w2_zp, E_global) -> bool:

@@ -400,3 +400,60 @@ def test_ep_dispatch_and_combine_kernels_vs_torch(w4):
         ref = ref + tw[s, None] * back[row[s]].float()
     ref = ref + sh.float()
     assert torch.equal(out, ref)
+
+
+def test_fused_decode_layer_skips_invalid_ids(w4):
+    """Slots whose expert id is -1 or >= E contribute nothing (the reference's align skips
+    them); a token with no valid slot gets a zero row."""
+    T, E, k = 24, 64, 8
+    c = I.moe_layer_case(808, T, E, 2048, 512, k, 128)
+    ids = c["topk_ids"].copy()
+    ids[3, 2] = -1
+    ids[5, 0] = E
+    ids[7, :] = -1
+    w = c["topk_weights"].copy()
+    y = torch.ops.w4a8_b200.moe_decode(cu(c["x"]), cu(O.pack_int4(c["c13"])), cu(c["s13"]),
+                                       cu(O.pack_zeros(c["z13"])), cu(O.pack_int4(c["c2"])),
+                                       cu(c["s2"]), cu(O.pack_zeros(c["z2"])), cu(w), cu(ids))
+    keep = (ids >= 0) & (ids < E)
+    ids_o = np.where(keep, ids, 0)
+    w_o = np.where(keep, w, 0.0).astype(np.float32)
+    ref = O.moe_layer(c["x"], O.pack_int4(c["c13"]), c["s13"], O.pack_zeros(c["z13"]),
+                      O.pack_int4(c["c2"]), c["s2"], O.pack_zeros(c["z2"]), ids_o, w_o)
+    yn = y.float().cpu().numpy()
+    assert np.all(yn[7] == 0)
+    assert max_abs_rel(yn, ref) <= MAX_ABS_REL
+
+
+@pytest.mark.parametrize("gate_up,asym", [(True, True), (False, True), (True, False)])
+def test_stream_pack_matches_layout_restatement(w4, gate_up, asym):
+    """The load-time prepack kernel writes exactly the block layout the oracle restates."""
+    rng = np.random.default_rng(830)
+    E, N, K = 3, (256 if gate_up else 256), 1024
+    w = rng.integers(-2 ** 31, 2 ** 31 - 1, (E, N, K // 8), dtype=np.int64).astype(np.int32)
+    s = rng.uniform(1e-3, 2e-2, (E, N, K // 128)).astype(np.float16)
+    z = rng.integers(-2 ** 31, 2 ** 31 - 1, (E, N // 8, K // 128), dtype=np.int64).astype(np.int32) if asym else None
+    zt = cu(z) if asym else torch.empty(0, dtype=torch.int32, device="cuda")
+    p = torch.ops.w4a8_b200.stream_pack(cu(w), cu(s), zt, gate_up).cpu().numpy()
+    assert np.array_equal(p, O.stream_pack(w, s, z, gate_up))
+
+
+@pytest.mark.parametrize("T,E,asym", [(1, 64, True), (32, 257, True), (32, 64, False), (96, 64, True)])
+def test_packed_decode_layer_equals_unpacked(w4, T, E, asym):
+    """moe_decode_packed on prepacked weights gives the op-layout moe_decode's output bit for
+    bit (same arithmetic, same order), and is within the bar of the oracle."""
+    c = I.moe_layer_case(1700 + T + E, T, E, 2048, 512, 8, 128, asym=asym)
+    z1 = cu(O.pack_zeros(c["z13"])) if asym else torch.empty(0, dtype=torch.int32, device="cuda")
+    z2 = cu(O.pack_zeros(c["z2"])) if asym else torch.empty(0, dtype=torch.int32, device="cuda")
+    w1, w2 = cu(O.pack_int4(c["c13"])), cu(O.pack_int4(c["c2"]))
+    s1, s2 = cu(c["s13"]), cu(c["s2"])
+    tw, ids = cu(c["topk_weights"]), cu(c["topk_ids"])
+    y = torch.ops.w4a8_b200.moe_decode(cu(c["x"]), w1, s1, z1, w2, s2, z2, tw, ids)
+    p13 = torch.ops.w4a8_b200.stream_pack(w1, s1, z1, True)
+    p2 = torch.ops.w4a8_b200.stream_pack(w2, s2, z2, False)
+    yp = torch.ops.w4a8_b200.moe_decode_packed(cu(c["x"]), p13, p2, E, 512, tw, ids)
+    assert torch.equal(y.view(torch.int16), yp.view(torch.int16))
+    ref = O.moe_layer(c["x"], O.pack_int4(c["c13"]), c["s13"], O.pack_zeros(c["z13"]) if asym else None,
+                      O.pack_int4(c["c2"]), c["s2"], O.pack_zeros(c["z2"]) if asym else None,
+                      c["topk_ids"], c["topk_weights"])
+    assert max_abs_rel(yp.float().cpu().numpy(), ref) <= MAX_ABS_REL
