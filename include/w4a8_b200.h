@@ -206,24 +206,44 @@ W4A8_API int w4a8_silu_and_mul(const void* x, void* out, int64_t M, int64_t inte
 /*
  * Expert-parallel dispatch (no counterpart in the reference, which has no expert parallelism;
  * its expert_map is only forwarded to vLLM's align, w4a8_fp8_wmma/w4a8_fp8_wmma/
- * moe_experts.py:587-589). Slot s = t*top_k + j goes to rank d = topk_ids[s] / experts_per_rank
- * (clamped to [0, world)) at send row d*capacity + (number of earlier slots bound for d):
- * send_x[row] = x[t] (fp16, H), send_id[row] = topk_ids[s] - d*experts_per_rank (local expert),
- * slot_row[s] = row. Unclaimed rows get send_id -1. capacity >= T*top_k; graph-capturable.
+ * moe_experts.py:587-589). Each of the T tokens is quantised once (the oracle's per-token e4m3
+ * rounding) and written once per rank that owns one of its top_k experts (rank d owns global
+ * experts [d*experts_per_rank, (d+1)*experts_per_rank)), as one payload row of
+ * w4a8_ep_row_bytes(H, top_k) bytes:
+ *   [H e4m3 bytes][H/128 fp32 group sums][fp32 scale][top_k int32 local ids][top_k fp32 weights]
+ * (local id -1 = that slot is on another rank). send_rows is (world, T) rows: chunk d holds
+ * rank d's rows in token order; rows no token claims get ids -1. pos (world, T) int32 receives
+ * each token's row in chunk d or -1. own_rows (T rows, or NULL) receives every token once more
+ * with the single slot shared_local_id at weight 1 (a replicated shared expert). Ids outside
+ * [0, world*experts_per_rank) are dropped. H % 256 == 0, top_k <= 16, world <= 32.
  */
-W4A8_API int w4a8_ep_dispatch(const void* x, const int32_t* topk_ids, int64_t T, int64_t top_k,
-                              int64_t H, int32_t experts_per_rank, int32_t world,
-                              int64_t capacity, void* send_x, int32_t* send_id,
-                              int32_t* slot_row, w4a8_stream_t stream);
+W4A8_API size_t w4a8_ep_row_bytes(int64_t H, int64_t top_k);
+W4A8_API int w4a8_ep_pack(const void* x, const int32_t* topk_ids, const float* topk_weights,
+                          int64_t T, int64_t top_k, int64_t H, int32_t experts_per_rank,
+                          int32_t world, int32_t shared_local_id, void* send_rows,
+                          void* own_rows, int32_t* pos, w4a8_stream_t stream);
 
 /*
- * Expert-parallel combine: out[t, n] = sum_{j ascending} w[t*top_k+j] * back[slot_row[t*top_k+j], n]
- * (fp32; fp16 back rows), plus fp32(shared[t, n]) when `shared` (fp16 (T, H)) is not NULL.
- * The arithmetic of mmq_fp8_moe_gather_reduce followed by the shared-expert add.
+ * The gated MoE layer on R payload rows (received rows, then the own shared-expert rows): for
+ * every row, out[r] = sum over its valid local slots j (ascending) of
+ * w_j * fp16(down_e(silu_and_mul(gate_up_e(row)))) in fp32, with the expert weights prepacked
+ * by w4a8_stream_pack (E local experts). out is (R, H) fp32; rows without a valid slot are 0.
+ * Same arithmetic as w4a8_moe_decode. Workspace: w4a8_ep_moe_rows_workspace_size.
  */
-W4A8_API int w4a8_ep_combine(const void* back, const int32_t* slot_row,
-                             const float* topk_weights, const void* shared, float* out,
-                             int64_t T, int64_t top_k, int64_t H, w4a8_stream_t stream);
+W4A8_API size_t w4a8_ep_moe_rows_workspace_size(int64_t R, int64_t top_k, int64_t E, int64_t H,
+                                                int64_t I);
+W4A8_API int w4a8_ep_moe_rows(const void* rows, int64_t R, int64_t top_k, int64_t E,
+                              const void* p13, const void* p2, int64_t H, int64_t I, float* out,
+                              void* workspace, size_t workspace_bytes, w4a8_stream_t stream);
+
+/*
+ * Expert-parallel gather: out[t] = sum over ranks d ascending with pos[d, t] >= 0 of
+ * back[d*T + pos[d, t]] (fp32 rows returned by the owners), then + own_out[t] (the shared
+ * expert's fp32 row) when own_out is not NULL. out is (T, H) fp32.
+ */
+W4A8_API int w4a8_ep_gather(const float* back, const int32_t* pos, const float* own_out,
+                            float* out, int64_t T, int32_t world, int64_t H,
+                            w4a8_stream_t stream);
 
 /*
  * Whole gated MoE layer at decode sizes in one call: moe_align (block 8) -> gate_up GEMV ->

@@ -32,6 +32,10 @@ int launch_fused_decode(const void* x, const int32_t* topk_ids, const float* top
                         const int32_t* z13, const int32_t* w2, const void* s2, const int32_t* z2,
                         int64_t H, int64_t I, void* out, void* workspace, cudaStream_t st,
                         const void* p13 = nullptr, const void* p2 = nullptr);
+// The same layer on expert-parallel payload rows (w4a8_ep_pack layout); fp32 (R, H) output.
+int launch_fused_decode_rows(const void* rows, int64_t row_bytes, int64_t R, int64_t top_k,
+                             int64_t E, const void* p13, const void* p2, int64_t H, int64_t I,
+                             float* out, void* workspace, cudaStream_t st);
 size_t stream_pack_bytes(int64_t E, int64_t N, int64_t K);
 int launch_stream_pack(const int32_t* w, const void* scales, const int32_t* zeros, int64_t E,
                        int64_t N, int64_t K, int gate_up, void* packed, cudaStream_t st);

@@ -46,6 +46,7 @@
 #include "gemm_common.h"
 #include "internal.h"
 #include "sm100.cuh"
+#include "e4_operand.cuh"
 #include "stream_core.cuh"
 
 namespace w4a8 {
@@ -68,9 +69,14 @@ enum DecMode : int { kGateUp = 0, kDown = 1 };
 enum : int { kMetaActive = 0, kMetaUnit1 = 1, kMetaUnit2 = 2, kMetaErr = 3, kMetaWords = 4 };
 
 struct DecArgs {
-    const int32_t* topk_ids;   // (T, top_k)
-    const float* topk_w;       // (T, top_k)
+    const int32_t* topk_ids;   // row t's slot j at topk_ids[t * ids_stride + j]
+    const float* topk_w;       // row t's weight j at topk_w[t * ids_stride + j]
     int T, top_k, E;
+    int ids_stride;            // elements between rows of topk_ids / topk_w (top_k when dense)
+    int64_t xe_stride;         // bytes between gate_up operand rows (K when dense)
+    int64_t xs_stride;         // floats between rows of the group sums (K/128 when dense)
+    int64_t asc_stride;        // floats between activation scales (1 when dense)
+    int out_f32;               // the layer output is fp32 (else fp16)
     int32_t* off;              // [E + 1] sorted-row offset of each expert
     int32_t* active;           // [E] experts with rows, heavy (> kDMaxRows rows) first
     int32_t* meta;             // kMeta*
@@ -93,87 +99,13 @@ struct DecArgs {
     const float* asc;          // per-row activation scale
     __half* silu;              // (S, I) fp16 SiLU rows (gate_up output)
     __half* out2;              // (S, H) fp16 down rows
-    __half* out;               // (T, H) fp16 layer output
+    void* out;                 // (T, H) layer output, fp16 or fp32 (out_f32)
     const __half* x;           // (T, H) fp16 input (prep)
 };
 
 // ---------------------------------------------------------------------------------------
 // Launch 1: routing sort + token quantisation.
 // ---------------------------------------------------------------------------------------
-// e4m3 operand of one row: the oracle's rounding (scale = max(amax, 4.48e-6) / 448 and
-// q = e4m3_rn(x / scale), IEEE divides; w4a8_fp8_wmma/test_correctness.py:74-76), bytes stored
-// in the GEMV's order (per 8-element unit: elements 0,2,4,6 then 1,3,5,7), the per 128-group
-// sums S of the e4m3 values, and the scale. WARP: one warp per row reading memory written by
-// other CTAs of the same launch (L2 loads); else the whole block. K % 256 == 0.
-template <bool WARP>
-__device__ void quant_row_e4(const __half* src, int K, int64_t row, uint8_t* xe, float* xs,
-                             float* scale, float* red) {
-    const int n_thr = WARP ? 32 : (int)blockDim.x;
-    const int tid = WARP ? (int)(threadIdx.x & 31) : (int)threadIdx.x;
-    const int nch = K / 8;
-    auto ld = [&](int i) {
-        return WARP ? __ldcg(reinterpret_cast<const uint4*>(src) + i)
-                    : *reinterpret_cast<const uint4*>(src + (int64_t)i * 8);
-    };
-    float amax = 0.f;
-    for (int i = tid; i < nch; i += n_thr) {
-        const uint4 v = ld(i);
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const __half2 h = __habs2(*reinterpret_cast<const __half2*>(&w[j]));
-            amax = fmaxf(amax, fmaxf(__low2float(h), __high2float(h)));
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    if (!WARP) {
-        const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-        if (l == 0) red[w] = amax;
-        __syncthreads();
-        if (w == 0) {
-            float v = l < (int)(blockDim.x >> 5) ? red[l] : 0.f;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-            if (l == 0) red[0] = v;
-        }
-        __syncthreads();
-        amax = red[0];
-    }
-    const float s = __fdiv_rn(fmaxf(amax, kAmaxFloor), kE4m3Max);
-    if (tid == 0) scale[row] = s;
-    const int G = K / 128;
-    for (int i0 = 0; i0 < nch; i0 += n_thr) {  // lanes 0-15 / 16-31 of a warp: one group each
-        const int i = i0 + tid;
-        float sum = 0.f;
-        if (i < nch) {
-            const uint4 v = ld(i);
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-            uint32_t q[2];
-#pragma unroll
-            for (int j = 0; j < 4; j += 2) {
-                const __half2 h0 = *reinterpret_cast<const __half2*>(&w[j]);
-                const __half2 h1 = *reinterpret_cast<const __half2*>(&w[j + 1]);
-                const uint16_t p0 = f32x2_to_e4m3x2(__fdiv_rn(__low2float(h0), s),
-                                                    __fdiv_rn(__high2float(h0), s));
-                const uint16_t p1 = f32x2_to_e4m3x2(__fdiv_rn(__low2float(h1), s),
-                                                    __fdiv_rn(__high2float(h1), s));
-                q[j / 2] = (uint32_t)p0 | ((uint32_t)p1 << 16);
-                const uint32_t e0 = e4m3x2_to_f16x2(p0), e1 = e4m3x2_to_f16x2(p1);
-                const float2 d0 = __half22float2(*reinterpret_cast<const __half2*>(&e0));
-                const float2 d1 = __half22float2(*reinterpret_cast<const __half2*>(&e1));
-                sum += (d0.x + d0.y) + (d1.x + d1.y);
-            }
-            // natural bytes q0..q7 -> GEMV order q0 q2 q4 q6 | q1 q3 q5 q7
-            reinterpret_cast<uint2*>(xe + row * K)[i] =
-                make_uint2(prmt(q[0], q[1], 0x6420u), prmt(q[0], q[1], 0x7531u));
-        }
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if ((tid & 15) == 0 && i < nch) xs[row * G + i / 16] = sum;
-    }
-}
-
 // Exclusive scan of v over the block (kPrepThreads threads, one value each); returns the
 // prefix and writes the total to *total.
 __device__ __forceinline__ int block_excl_scan(int v, int* red, int* total) {
@@ -225,14 +157,15 @@ __global__ void __launch_bounds__(kPrepThreads) decode_prep_kernel(const DecArgs
     for (int i = tid; i < a.T * n16; i += kPrepThreads) a.tok_done[i] = 0;
     for (int i = tid; i < S; i += kPrepThreads) a.amax[i] = 0.f;
     __syncthreads();
+    auto slot_id = [&](int s) { return a.topk_ids[(int64_t)(s / a.top_k) * a.ids_stride + s % a.top_k]; };
     for (int s = tid; s < S; s += kPrepThreads) {
-        const int e = a.topk_ids[s];
+        const int e = slot_id(s);
         if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
     }
     for (int t = tid; t < a.T; t += kPrepThreads) {
         int n = 0;
         for (int j = 0; j < a.top_k; ++j) {
-            const int e = a.topk_ids[t * a.top_k + j];
+            const int e = a.topk_ids[(int64_t)t * a.ids_stride + j];
             n += (e >= 0 && e < E);
         }
         a.nslot[t] = n;
@@ -275,7 +208,7 @@ __global__ void __launch_bounds__(kPrepThreads) decode_prep_kernel(const DecArgs
     const int lane = tid & 31, warp = tid >> 5;
     for (int c0 = 0; c0 < S; c0 += kPrepThreads) {
         const int s = c0 + tid;
-        int e = s < S ? a.topk_ids[s] : -1;
+        int e = s < S ? slot_id(s) : -1;
         if (!(e >= 0 && e < E)) e = -1;
         if (s < S && e < 0) a.slot_pos[s] = -1;
         for (int w = 0; w < kPrepThreads / 32; ++w) {
@@ -300,7 +233,10 @@ __global__ void __launch_bounds__(kPrepThreads) decode_prep_kernel(const DecArgs
     // tokens without a valid slot: the layer output is zero
     for (int t = 0; t < a.T; ++t)
         if (ns[t] == 0)
-            for (int n = tid; n < a.H; n += kPrepThreads) a.out[(int64_t)t * a.H + n] = __float2half_rn(0.f);
+            for (int n = tid; n < a.H; n += kPrepThreads) {
+                if (a.out_f32) static_cast<float*>(a.out)[(int64_t)t * a.H + n] = 0.f;
+                else static_cast<__half*>(a.out)[(int64_t)t * a.H + n] = __float2half_rn(0.f);
+            }
 }
 
 // The first three members are one packed weight block (w4a8_stream_pack): a stage of packed
@@ -401,9 +337,9 @@ __device__ __forceinline__ void dec_produce(const DecArgs& a, DSmem& sm, const C
     }
     __syncwarp();  // expect_tx precedes every lane's bulk copy
     if (MODE == kGateUp && lane < nrows) {
-        bulk_load(&S.act[lane][0], a.xe + (int64_t)src * a.K + (int64_t)chunk * kDSpi * 128,
+        bulk_load(&S.act[lane][0], a.xe + (int64_t)src * a.xe_stride + (int64_t)chunk * kDSpi * 128,
                   kDSpi * 128, &sm.full[st]);
-        bulk_load(&S.xs[lane][0], a.xsum + (int64_t)src * a.G + chunk * kDSpi, kDSpi * 4,
+        bulk_load(&S.xs[lane][0], a.xsum + (int64_t)src * a.xs_stride + chunk * kDSpi, kDSpi * 4,
                   &sm.full[st]);
     }
     if (PACKED) {
@@ -565,7 +501,7 @@ __device__ __forceinline__ void combine_pair(const DecArgs& a, int t, int n) {
         for (int q = 0; q < 4; ++q) {
             const bool ok = j0 + q < a.top_k;
             pos[q] = ok ? __ldg(a.slot_pos + t * a.top_k + j0 + q) : -1;
-            wt[q] = ok ? __ldg(a.topk_w + t * a.top_k + j0 + q) : 0.f;
+            wt[q] = ok ? __ldg(a.topk_w + (int64_t)t * a.ids_stride + j0 + q) : 0.f;
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q)
@@ -580,7 +516,12 @@ __device__ __forceinline__ void combine_pair(const DecArgs& a, int t, int n) {
             }
         }
     }
-    *reinterpret_cast<__half2*>(a.out + (int64_t)t * a.H + n) = __floats2half2_rn(acc0, acc1);
+    if (a.out_f32)
+        *reinterpret_cast<float2*>(static_cast<float*>(a.out) + (int64_t)t * a.H + n) =
+            make_float2(acc0, acc1);
+    else
+        *reinterpret_cast<__half2*>(static_cast<__half*>(a.out) + (int64_t)t * a.H + n) =
+            __floats2half2_rn(acc0, acc1);
 }
 
 template <int MODE, bool PACKED>
@@ -723,7 +664,7 @@ decode_gemv_kernel(const DecArgs a, const __grid_constant__ CUtensorMap tmw) {
                         const int rl = tg * 8 + 2 * c + q;
                         if (rl < nrows)
                             asc_c[tg][q] = MODE == kGateUp
-                                               ? __ldg(a.asc + __ldg(a.sorted_tok + p0 + rl))
+                                               ? __ldg(a.asc + __ldg(a.sorted_tok + p0 + rl) * a.asc_stride)
                                                : sm.st[st].asc[rl];
                     }
                 if (MODE == kDown && lane < nrows) my_t = __ldg(a.sorted_tok + p0 + lane);
@@ -945,11 +886,52 @@ int launch_stream_pack(const int32_t* w, const void* scales, const int32_t* zero
     return launch_status();
 }
 
+namespace {
+// Operand source of the gate_up launch: fp16 token rows quantised by the prep launch, or
+// expert-parallel payload rows that already hold the e4m3 operand (w4a8_ep_pack).
+struct DecInput {
+    const void* x;             // fp16 (T, H) or payload rows
+    int64_t row_bytes;         // 0: fp16 rows; else payload row size
+    const int32_t* topk_ids;
+    const float* topk_w;
+};
+int run_fused_decode(const DecInput& in, int64_t T, int64_t top_k, int64_t E,
+                     const int32_t* w13, const void* s13, const int32_t* z13, const int32_t* w2,
+                     const void* s2, const int32_t* z2, int64_t H, int64_t I, void* out,
+                     bool out_f32, void* workspace, cudaStream_t st, const void* p13,
+                     const void* p2);
+}  // namespace
+
 int launch_fused_decode(const void* x, const int32_t* topk_ids, const float* topk_weights,
                         int64_t T, int64_t top_k, int64_t E, const int32_t* w13, const void* s13,
                         const int32_t* z13, const int32_t* w2, const void* s2, const int32_t* z2,
                         int64_t H, int64_t I, void* out, void* workspace, cudaStream_t st,
                         const void* p13, const void* p2) {
+    return run_fused_decode(DecInput{x, 0, topk_ids, topk_weights}, T, top_k, E, w13, s13, z13,
+                            w2, s2, z2, H, I, out, false, workspace, st, p13, p2);
+}
+
+int launch_fused_decode_rows(const void* rows, int64_t row_bytes, int64_t R, int64_t top_k,
+                             int64_t E, const void* p13, const void* p2, int64_t H, int64_t I,
+                             float* out, void* workspace, cudaStream_t st) {
+    const int64_t G = H / 128;
+    const uint8_t* b = static_cast<const uint8_t*>(rows);
+    const int64_t off_ids = H + 4 * G + 4;
+    return run_fused_decode(DecInput{rows, row_bytes, reinterpret_cast<const int32_t*>(b + off_ids),
+                                     reinterpret_cast<const float*>(b + off_ids + 4 * top_k)},
+                            R, top_k, E, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, H,
+                            I, out, true, workspace, st, p13, p2);
+}
+
+namespace {
+int run_fused_decode(const DecInput& in, int64_t T, int64_t top_k, int64_t E,
+                     const int32_t* w13, const void* s13, const int32_t* z13, const int32_t* w2,
+                     const void* s2, const int32_t* z2, int64_t H, int64_t I, void* out,
+                     bool out_f32, void* workspace, cudaStream_t st, const void* p13,
+                     const void* p2) {
+    const void* x = in.x;
+    const int32_t* topk_ids = in.topk_ids;
+    const float* topk_weights = in.topk_w;
     static_assert(sizeof(DSmem) + 1024 <= 227 * 1024, "decode GEMV shared memory");
     const DecLayout L = dec_layout(T, top_k, E, H, I);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -973,17 +955,34 @@ int launch_fused_decode(const void* x, const int32_t* topk_ids, const float* top
     a.I = (int)I;
     a.silu = reinterpret_cast<__half*>(ws + L.off_silu);
     a.out2 = reinterpret_cast<__half*>(ws + L.off_out2);
-    a.out = static_cast<__half*>(out);
+    a.out = out;
+    a.out_f32 = out_f32 ? 1 : 0;
     a.x = static_cast<const __half*>(x);
-    // 1. routing sort + token quantisation
-    a.xe = ws + L.off_xh1;
-    a.xsum = reinterpret_cast<const float*>(ws + L.off_xs1);
-    a.asc = reinterpret_cast<const float*>(ws + L.off_sc1);
+    const int64_t G1 = H / 128;
+    if (in.row_bytes == 0) {
+        a.ids_stride = (int)top_k;
+        a.xe = ws + L.off_xh1;
+        a.xsum = reinterpret_cast<const float*>(ws + L.off_xs1);
+        a.asc = reinterpret_cast<const float*>(ws + L.off_sc1);
+        a.xe_stride = H;
+        a.xs_stride = G1;
+        a.asc_stride = 1;
+    } else {  // payload rows: [H e4m3 bytes][G sums][scale][top_k ids][top_k weights]
+        a.ids_stride = (int)(in.row_bytes / 4);
+        const uint8_t* b = static_cast<const uint8_t*>(x);
+        a.xe = b;
+        a.xsum = reinterpret_cast<const float*>(b + H);
+        a.asc = reinterpret_cast<const float*>(b + H + 4 * G1);
+        a.xe_stride = in.row_bytes;
+        a.xs_stride = in.row_bytes / 4;
+        a.asc_stride = in.row_bytes / 4;
+    }
+    // 1. routing sort (+ token quantisation of fp16 input rows)
     const size_t prep_smem = (size_t)E * 8 + (size_t)T * 4;
     if (prep_smem > 48 * 1024)
         cudaFuncSetAttribute(decode_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)prep_smem);
-    decode_prep_kernel<<<(unsigned)(1 + T), kPrepThreads, prep_smem, st>>>(a);
+    decode_prep_kernel<<<(unsigned)(1 + (in.row_bytes ? 0 : T)), kPrepThreads, prep_smem, st>>>(a);
     if (int rc = launch_status()) return rc;
     // 2. gate_up GEMV + SiLU (+ the down operand, by each expert's last unit)
     a.packed = static_cast<const uint8_t*>(p13);
@@ -1010,5 +1009,6 @@ int launch_fused_decode(const void* x, const int32_t* topk_ids, const float* top
     a.asc = nullptr;
     return launch_dec_gemv<kDown>(a, (int)std::min<int64_t>(max_active * (H / 128), 1 << 30), st);
 }
+}  // namespace
 
 }  // namespace w4a8

@@ -307,53 +307,73 @@ at::Tensor silu_and_mul_forward(const at::Tensor& x) {
     return out;
 }
 
-std::vector<at::Tensor> ep_dispatch_forward(const at::Tensor& x, const at::Tensor& topk_ids,
-                                            int64_t experts_per_rank, int64_t world,
-                                            int64_t capacity) {
+std::vector<at::Tensor> ep_pack_forward(const at::Tensor& x, const at::Tensor& topk_ids,
+                                        const at::Tensor& topk_weights, int64_t experts_per_rank,
+                                        int64_t world, int64_t shared_local_id) {
     TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kHalf && x.dim() == 2 && x.is_contiguous(),
                 "x must be a contiguous (T, H) fp16 CUDA tensor");
-    TORCH_CHECK(topk_ids.is_cuda() && topk_ids.scalar_type() == at::kInt &&
-                    topk_ids.is_contiguous() && topk_ids.dim() == 2 &&
-                    topk_ids.size(0) == x.size(0),
-                "topk_ids must be a contiguous (T, top_k) int32 CUDA tensor");
+    TORCH_CHECK(topk_ids.scalar_type() == at::kInt && topk_ids.is_contiguous() &&
+                    topk_ids.dim() == 2 && topk_ids.size(0) == x.size(0) &&
+                    topk_weights.scalar_type() == at::kFloat && topk_weights.is_contiguous() &&
+                    topk_weights.sizes() == topk_ids.sizes(),
+                "topk_ids (T, k) int32 / topk_weights (T, k) fp32 must be contiguous");
     const c10::cuda::CUDAGuard guard(x.device());
     const int64_t T = x.size(0), H = x.size(1), k = topk_ids.size(1);
-    auto send_x = at::empty({world * capacity, H}, x.options());
-    auto send_id = at::empty({world * capacity}, topk_ids.options());
-    auto slot_row = at::empty({T * k}, topk_ids.options());
-    check_status(w4a8_ep_dispatch(x.data_ptr(), topk_ids.data_ptr<int32_t>(), T, k, H,
-                                  (int32_t)experts_per_rank, (int32_t)world, capacity,
-                                  send_x.data_ptr(), send_id.data_ptr<int32_t>(),
-                                  slot_row.data_ptr<int32_t>(), cur_stream()),
-                 "ep_dispatch");
-    return {send_x, send_id, slot_row};
+    const int64_t rb = (int64_t)w4a8_ep_row_bytes(H, k);
+    // rows [0, world*T): the send chunks; [world*T, (world+1)*T): the own shared-expert rows
+    auto rows = at::empty({(world + 1) * T, rb}, x.options().dtype(at::kByte));
+    auto pos = at::empty({world, T}, topk_ids.options());
+    uint8_t* base = rows.data_ptr<uint8_t>();
+    check_status(w4a8_ep_pack(x.data_ptr(), topk_ids.data_ptr<int32_t>(),
+                              topk_weights.data_ptr<float>(), T, k, H, (int32_t)experts_per_rank,
+                              (int32_t)world, (int32_t)shared_local_id, base,
+                              shared_local_id >= 0 ? base + world * T * rb : nullptr,
+                              pos.data_ptr<int32_t>(), cur_stream()),
+                 "ep_pack");
+    return {rows, pos};
 }
 
-at::Tensor ep_combine_forward(const at::Tensor& back, const at::Tensor& slot_row,
-                              const at::Tensor& topk_weights, const c10::optional<at::Tensor>& shared,
-                              int64_t top_k) {
-    TORCH_CHECK(back.is_cuda() && back.scalar_type() == at::kHalf && back.dim() == 2 &&
+at::Tensor ep_moe_rows_forward(const at::Tensor& rows, const at::Tensor& p13, const at::Tensor& p2,
+                               int64_t E, int64_t H, int64_t I, int64_t top_k) {
+    TORCH_CHECK(rows.is_cuda() && rows.scalar_type() == at::kByte && rows.dim() == 2 &&
+                    rows.is_contiguous() && (size_t)rows.size(1) == w4a8_ep_row_bytes(H, top_k),
+                "rows must be contiguous (R, ep_row_bytes) uint8 payload rows");
+    TORCH_CHECK(p13.scalar_type() == at::kByte && p2.scalar_type() == at::kByte &&
+                    (size_t)p13.numel() == w4a8_stream_pack_size(E, 2 * I, H) &&
+                    (size_t)p2.numel() == w4a8_stream_pack_size(E, H, I),
+                "p13 / p2 must be stream_pack outputs for (E, 2*inter, hidden) / (E, hidden, inter)");
+    const c10::cuda::CUDAGuard guard(rows.device());
+    const int64_t R = rows.size(0);
+    auto out = at::empty({R, H}, rows.options().dtype(at::kFloat));
+    auto ws = workspace(rows, w4a8_ep_moe_rows_workspace_size(R, top_k, E, H, I));
+    check_status(w4a8_ep_moe_rows(rows.data_ptr(), R, top_k, E, p13.data_ptr(), p2.data_ptr(), H,
+                                  I, out.data_ptr<float>(), ws.data_ptr(), (size_t)ws.numel(),
+                                  cur_stream()),
+                 "ep_moe_rows");
+    return out;
+}
+
+at::Tensor ep_gather_forward(const at::Tensor& back, const at::Tensor& pos,
+                             const c10::optional<at::Tensor>& own_out) {
+    TORCH_CHECK(back.is_cuda() && back.scalar_type() == at::kFloat && back.dim() == 2 &&
                     back.is_contiguous(),
-                "back must be a contiguous (rows, H) fp16 CUDA tensor");
-    TORCH_CHECK(slot_row.scalar_type() == at::kInt && slot_row.is_contiguous() &&
-                    topk_weights.scalar_type() == at::kFloat && topk_weights.is_contiguous() &&
-                    topk_weights.numel() == slot_row.numel() && top_k > 0 &&
-                    slot_row.numel() % top_k == 0,
-                "slot_row int32 / topk_weights fp32 must be contiguous with T*top_k entries");
+                "back must be a contiguous (world*T, H) fp32 CUDA tensor");
+    TORCH_CHECK(pos.scalar_type() == at::kInt && pos.is_contiguous() && pos.dim() == 2 &&
+                    pos.size(0) * pos.size(1) == back.size(0),
+                "pos must be a contiguous (world, T) int32 tensor");
     const c10::cuda::CUDAGuard guard(back.device());
-    const int64_t T = slot_row.numel() / top_k, H = back.size(1);
-    const void* sh = nullptr;
-    if (shared.has_value() && shared->defined()) {
-        TORCH_CHECK(shared->scalar_type() == at::kHalf && shared->is_contiguous() &&
-                        shared->size(0) == T && shared->size(1) == H,
-                    "shared must be a contiguous (T, H) fp16 tensor");
-        sh = shared->data_ptr();
+    const int64_t W = pos.size(0), T = pos.size(1), H = back.size(1);
+    const float* own = nullptr;
+    if (own_out.has_value() && own_out->defined()) {
+        TORCH_CHECK(own_out->scalar_type() == at::kFloat && own_out->is_contiguous() &&
+                        own_out->size(0) == T && own_out->size(1) == H,
+                    "own_out must be a contiguous (T, H) fp32 tensor");
+        own = own_out->data_ptr<float>();
     }
-    auto out = at::empty({T, H}, back.options().dtype(at::kFloat));
-    check_status(w4a8_ep_combine(back.data_ptr(), slot_row.data_ptr<int32_t>(),
-                                 topk_weights.data_ptr<float>(), sh, out.data_ptr<float>(), T,
-                                 top_k, H, cur_stream()),
-                 "ep_combine");
+    auto out = at::empty({T, H}, back.options());
+    check_status(w4a8_ep_gather(back.data_ptr<float>(), pos.data_ptr<int32_t>(), own,
+                                out.data_ptr<float>(), T, (int32_t)W, H, cur_stream()),
+                 "ep_gather");
     return out;
 }
 
@@ -491,8 +511,11 @@ TORCH_LIBRARY_IMPL(w4a8_fp8_wmma, CUDA, m) {
 TORCH_LIBRARY(w4a8_b200, m) {
     m.def("act_quant_fp8(Tensor x) -> Tensor[]");
     m.def("silu_and_mul(Tensor x) -> Tensor");
-    m.def("ep_dispatch(Tensor x, Tensor topk_ids, int experts_per_rank, int world, int capacity) -> Tensor[]");
-    m.def("ep_combine(Tensor back, Tensor slot_row, Tensor topk_weights, Tensor? shared, int top_k) -> Tensor");
+    m.def("ep_pack(Tensor x, Tensor topk_ids, Tensor topk_weights, int experts_per_rank, int world, "
+          "int shared_local_id) -> Tensor[]");
+    m.def("ep_moe_rows(Tensor rows, Tensor p13, Tensor p2, int num_experts, int hidden, int inter, "
+          "int top_k) -> Tensor");
+    m.def("ep_gather(Tensor back, Tensor pos, Tensor? own_out) -> Tensor");
     // Whole gated MoE layer at decode sizes (align -> gate_up+SiLU -> down -> reduce).
     m.def("stream_pack(Tensor w, Tensor scales, Tensor zeros, bool gate_up) -> Tensor");
     m.def("moe_decode_packed(Tensor x, Tensor p13, Tensor p2, int num_experts, int inter, "
@@ -510,8 +533,9 @@ TORCH_LIBRARY(w4a8_b200, m) {
 TORCH_LIBRARY_IMPL(w4a8_b200, CUDA, m) {
     m.impl("act_quant_fp8", &act_quant_fp8_forward);
     m.impl("silu_and_mul", &silu_and_mul_forward);
-    m.impl("ep_dispatch", &ep_dispatch_forward);
-    m.impl("ep_combine", &ep_combine_forward);
+    m.impl("ep_pack", &ep_pack_forward);
+    m.impl("ep_moe_rows", &ep_moe_rows_forward);
+    m.impl("ep_gather", &ep_gather_forward);
     m.impl("moe_decode", &moe_decode_forward);
     m.impl("stream_pack", &stream_pack_forward);
     m.impl("moe_decode_packed", &moe_decode_packed_forward);

@@ -1,6 +1,7 @@
 """Expert-parallel dispatch/combine on CPU `gloo` ranks (world sizes 2 and 4), with an identity
 "expert" so the permutation logic is checked exactly; plus host-side failure cases: a rank
-that dies before the exchange and a rank holding the wrong expert shard raise instead of hang.
+that dies before the exchange, a rank holding the wrong expert shard, and ranks passing
+different token counts raise instead of hanging or corrupting rows.
 """
 import os
 import socket
@@ -45,10 +46,12 @@ def _worker_identity(rank, world, port, q):
             w = torch.rand(T, k)
             seen = []
 
-            def identity(rows, local_ids):
+            def identity(rows, local_ids, wts):
                 seen.append(int((local_ids >= 0).sum()))
                 assert torch.all(local_ids < E // world)
-                return rows  # the "expert" returns its input row
+                # every expert returns its input row: the row's result is its weight sum * row
+                wsum = torch.where(local_ids >= 0, wts, torch.zeros_like(wts)).sum(1, keepdim=True)
+                return wsum * rows.to(torch.float32)
 
             layer = ExpertParallelMoE(None, None, None, None, None, None, E, k, expert_fn=identity)
             out = layer(x, ids, w)
@@ -85,12 +88,14 @@ def test_ep_dispatch_combine_identity(world):
         assert ok and count_ok, (rank, ok, count_ok)
 
 
-def test_plan_dispatch_positions_are_stable_and_dense():
-    ids = torch.tensor([[0, 5], [4, 1], [7, 2]], dtype=torch.int32)  # E=8, 2 ranks -> 4 per rank
-    dest, pos, row = plan_dispatch(ids, 4, 2, capacity=6)
-    assert dest.tolist() == [0, 1, 1, 0, 1, 0]
-    assert pos.tolist() == [0, 0, 1, 1, 2, 2]
-    assert row.tolist() == [0, 6, 7, 1, 8, 2]
+def test_plan_dispatch_rows_are_stable_and_dense():
+    # E=8 over 2 ranks (4 each); token 2 has both slots on rank 0; id 9 is out of range
+    ids = torch.tensor([[0, 5], [4, 9], [3, 2], [6, 7]], dtype=torch.int32)
+    has, pos, local = plan_dispatch(ids, 4, 2)
+    assert has.tolist() == [[True, False, True, False], [True, True, False, True]]
+    assert pos.tolist() == [[0, -1, 1, -1], [0, 1, -1, 2]]
+    assert local[0].tolist() == [[0, -1], [-1, -1], [3, 2], [-1, -1]]
+    assert local[1].tolist() == [[-1, 1], [0, -1], [-1, -1], [2, 3]]
 
 
 def _worker_dies(rank, world, port, q):
@@ -99,7 +104,7 @@ def _worker_dies(rank, world, port, q):
         if rank == 1:
             os._exit(0)  # leaves before the exchange without a word
         layer = ExpertParallelMoE(None, None, None, None, None, None, 4, 1,
-                                  expert_fn=lambda r, i: r)
+                                  expert_fn=lambda r, i, w: r.float())
         try:
             layer(torch.zeros(2, 8, dtype=torch.float16), torch.tensor([[3], [2]], dtype=torch.int32),
                   torch.ones(2, 1))
@@ -136,3 +141,40 @@ def test_wrong_expert_shard_rejected():
     for rank, ok, _, err in res:
         assert err is None, err
         assert ok, rank
+
+
+def _worker_unequal_T(rank, world, port, q):
+    try:
+        _init(rank, world, port)
+        E, k, H = 8, 2, 16
+        T = 4 if rank == 0 else 6
+        x = torch.randn(T, H).to(torch.float16)
+        ids = torch.stack([torch.randperm(E)[:k] for _ in range(T)]).to(torch.int32)
+        w = torch.rand(T, k)
+
+        def identity(rows, local_ids, wts):
+            wsum = torch.where(local_ids >= 0, wts, torch.zeros_like(wts)).sum(1, keepdim=True)
+            return wsum * rows.to(torch.float32)
+        raised = False
+        try:
+            ExpertParallelMoE(None, None, None, None, None, None, E, k, expert_fn=identity)(x, ids, w)
+        except ValueError:
+            raised = True
+        # with a common max_tokens the same batches exchange correctly
+        layer = ExpertParallelMoE(None, None, None, None, None, None, E, k, expert_fn=identity,
+                                  max_tokens=8)
+        out = layer(x, ids, w)
+        ok = out.shape == (T, H) and bool(torch.allclose(out, w.sum(1, keepdim=True) * x.float(),
+                                                         rtol=1e-3, atol=1e-3))
+        q.put((rank, raised, ok, None))
+        dist.destroy_process_group()
+    except Exception:
+        q.put((rank, False, False, traceback.format_exc()))
+
+
+def test_unequal_token_counts_raise_or_pad():
+    res = _spawn(_worker_unequal_T, 2)
+    for rank, raised, ok, err in res:
+        assert err is None, err
+        assert raised, f"rank {rank}: unequal T was accepted"
+        assert ok, f"rank {rank}: max_tokens padding gave a wrong result"

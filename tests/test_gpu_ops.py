@@ -371,36 +371,48 @@ def test_silu_and_mul_exhaustive_fp16_gate(w4):
         assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
 
 
-def test_ep_dispatch_and_combine_kernels_vs_torch(w4):
-    """ep_dispatch / ep_combine against the torch statement of the same plan (plan_dispatch +
-    index copies + slot-order reduce): rows, local ids and slot rows are integer work and must
-    match exactly; the combine must equal the slot-order fmul/fadd sum plus the shared add."""
+def test_ep_pack_and_gather_kernels_vs_torch(w4):
+    """ep_pack against plan_dispatch and the oracle's quantisation: row positions, local ids and
+    weights are integer/copy work and must match exactly, the e4m3 bytes are the oracle's (in
+    the GEMV byte order), and ep_gather equals the rank-order fp32 sum plus the shared row."""
     from w4a8_fp8_wmma.ep import plan_dispatch
-    T, k, H, E, W = 24, 4, 256, 64, 4
+    T, k, H, E, W = 24, 4, 512, 64, 4
     rng = np.random.default_rng(77)
     ids = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
+    ids[3, 1] = E + 5  # out of range: dropped
     x = rng.standard_normal((T, H), dtype=np.float32).astype(np.float16)
-    C = T * k
-    xd, idd = cu(x), cu(ids)
-    send_x, send_id, slot_row = torch.ops.w4a8_b200.ep_dispatch(xd, idd, E // W, W, C)
-    dest, pos, row = plan_dispatch(idd, E // W, W, C)
-    assert torch.equal(slot_row.long(), row)
-    ref_id = torch.full((W * C,), -1, dtype=torch.int32, device="cuda")
-    ref_id[row] = (idd.reshape(-1).long() - dest * (E // W)).int()
-    assert torch.equal(send_id, ref_id)
-    slots = torch.arange(T * k, device="cuda")
-    assert torch.equal(send_x[row], xd[slots // k])
-    back = torch.randn((W * C, H), device="cuda").half()
-    tw = torch.rand(T * k, device="cuda")
-    sh = torch.randn((T, H), device="cuda").half()
-    out = torch.ops.w4a8_b200.ep_combine(back, slot_row, tw, sh, k)
+    w = rng.random((T, k), dtype=np.float32)
+    rows, pos = torch.ops.w4a8_b200.ep_pack(cu(x), cu(ids), cu(w), E // W, W, E // W)
+    has, pos_ref, local = plan_dispatch(cu(ids), E // W, W)
+    assert torch.equal(pos.long(), pos_ref)
+    G = H // 128
+    r = rows.cpu().numpy()
+    q, sc = O.act_quant(x)
+    perm = np.array([0, 2, 4, 6, 1, 3, 5, 7])
+    qg = q.reshape(T, H // 8, 8)[:, :, perm].reshape(T, H)
+    loc = local.cpu().numpy()
+    o = H + 4 * G + 4
+    for d in range(W):
+        for t in range(T):
+            p = int(pos_ref[d, t])
+            if p < 0:
+                continue
+            row = r[d * T + p]
+            assert np.array_equal(row[:H], qg[t])
+            assert row[H + 4 * G:o].view(np.float32)[0] == sc[t]
+            assert np.array_equal(row[o:o + 4 * k].view(np.int32), loc[d, t].astype(np.int32))
+            assert np.array_equal(row[o + 4 * k:o + 8 * k].view(np.float32),
+                                  np.where(loc[d, t] >= 0, w[t], 0).astype(np.float32))
+    own = r[W * T:]
+    assert np.all(own[:, o:o + 4].view(np.int32)[:, 0] == E // W)
+    back = torch.randn((W * T, H), device="cuda")
+    sh = torch.randn((T, H), device="cuda")
+    out = torch.ops.w4a8_b200.ep_gather(back, pos, sh)
     ref = torch.zeros((T, H), device="cuda")
-    for j in range(k):
-        s = torch.arange(T, device="cuda") * k + j
-        ref = ref + tw[s, None] * back[row[s]].float()
-    ref = ref + sh.float()
-    assert torch.equal(out, ref)
-
+    for d in range(W):
+        sel = pos_ref[d] >= 0
+        ref[sel] = ref[sel] + back[d * T + pos_ref[d][sel]]
+    assert torch.equal(out, ref + sh)
 
 def test_fused_decode_layer_skips_invalid_ids(w4):
     """Slots whose expert id is -1 or >= E contribute nothing (the reference's align skips

@@ -114,20 +114,28 @@ def test_align_validation():
 
 def test_ep_c_abi_validation():
     lib = load_lib()
-    d = lib.w4a8_ep_dispatch
+    rb = lib.w4a8_ep_row_bytes
+    rb.restype = c_sz
+    rb.argtypes = [c_i64, c_i64]
+    assert rb(2048, 8) == (2048 + 4 * 16 + 4 + 64 + 15) // 16 * 16
+    d = lib.w4a8_ep_pack
     d.restype = ctypes.c_int
-    d.argtypes = [c_vp, c_vp, c_i64, c_i64, c_i64, c_i32, c_i32, c_i64, c_vp, c_vp, c_vp, c_vp]
-    assert d(1, 1, 4, 2, 20, 8, 2, 8, 1, 1, 1, None) == -1          # H % 8 != 0
-    assert "multiple of 8" in _err(lib)
-    assert d(1, 1, 4, 2, 64, 8, 2, 7, 1, 1, 1, None) == -1          # capacity < T * top_k
-    assert "capacity" in _err(lib)
-    assert d(None, None, 0, 2, 64, 8, 2, 0, None, None, None, None) == 0   # T = 0: no-op
-    c = lib.w4a8_ep_combine
-    c.restype = ctypes.c_int
-    c.argtypes = [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp]
-    assert c(1, 1, 1, None, 1, 4, 17, 64, None) == -1              # top_k > 16
+    d.argtypes = [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp]
+    assert d(1, 1, 1, 4, 2, 200, 8, 2, -1, 1, None, 1, None) == -1   # H % 256 != 0
+    assert "multiple of 256" in _err(lib)
+    assert d(1, 1, 1, 4, 17, 256, 8, 2, -1, 1, None, 1, None) == -1  # top_k > 16
     assert "top_k" in _err(lib)
-    assert c(None, None, None, None, None, 0, 2, 64, None) == 0      # T = 0: no-op
+    assert d(None, None, None, 0, 2, 256, 8, 2, -1, None, None, None, None) == 0   # T = 0
+    g = lib.w4a8_ep_gather
+    g.restype = ctypes.c_int
+    g.argtypes = [c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i64, c_vp]
+    assert g(1, 1, None, 1, 4, 33, 64, None) == -1                 # world > 32
+    assert g(None, None, None, None, 0, 2, 64, None) == 0          # T = 0: no-op
+    m = lib.w4a8_ep_moe_rows
+    m.restype = ctypes.c_int
+    m.argtypes = [c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_sz, c_vp]
+    assert m(1, 4, 8, 33, 1, 1, 2000, 512, 1, 1, 1 << 20, None) == -1  # hidden % 512
+    assert "512" in _err(lib)
 
 
 def test_silu_and_mul_c_abi_validation():
