@@ -206,7 +206,7 @@ def run_ours(args):
 
         def step_fn():
             holder["y"] = layer(x, ids_r, tw_r)
-            recorded["rows"], recorded["ids"] = layer.last_recv
+            recorded["rows"] = layer.last_recv
     else:
         layer = None
         w13, s13, z13, w2, s2, z2 = make_layer(torch, dev, 1000, E_total)
@@ -255,8 +255,8 @@ def run_ours(args):
 
     # HBM bytes of the layer on this rank (max over ranks for the report).
     if world > 1:
-        rec_ids = recorded["ids"]
-        touched = int(torch.unique(rec_ids[rec_ids >= 0]).numel()) + 1  # + shared expert
+        rec_ids = payload_ids(torch, recorded["rows"])
+        touched = int(torch.unique(rec_ids[rec_ids >= 0]).numel())  # routed + shared (local)
     else:
         touched = len(np.unique(ids_np))
     touched_bytes = touched * EXPERT_BYTES
@@ -264,7 +264,7 @@ def run_ours(args):
     layer_bytes = touched_bytes + T * H * 2 * 2 + T * (TOP_K + 1) * 8
     flops = 2.0 * T * (TOP_K + 1) * (H * 2 * INTER + INTER * H)
     dom = dominant_kernel(torch, args, world, dist, dev, x, ids, w13, s13, z13, E_total, T,
-                          recorded if world > 1 else None, layer)
+                          recorded if world > 1 else tw, layer if world > 1 else (w2, s2, z2))
     e2e = end_to_end(torch, dist, args, world, dev, x_np, ids_np, w_np, layer, run_grouped_moe,
                      (w13, s13, z13, w2, s2, z2), E_total)
     if rank != 0:
@@ -319,15 +319,13 @@ def _max_over_ranks(torch, dist, world, dev, v):
 
 
 def launches_per_step(workload: str, world: int) -> int:
-    """Kernels of this library per step: decode = align count + place, operand quant, gate_up
-    GEMV + finish, down GEMV, gather-reduce (7); prefill = align count + place, then per GEMM
-    tc_quant_rows + w4_tc_kernel (2 x 2), inverse map + gather-reduce (8). EP runs the decode
-    layer once on the received rows plus the rank's own tokens (the shared expert rides along)
-    and adds the ep_dispatch and ep_combine kernels (9)."""
-    n = 7 if workload == "decode" else 8
+    """Kernels of this library per step: decode = decode_prep, gate_up GEMV, down GEMV (3);
+    prefill = align count + place, then per GEMM tc_quant_rows + w4_tc_kernel (2 x 2), inverse
+    map + gather-reduce (8). EP: ep_pack, the three decode-layer kernels on the payload rows,
+    ep_gather (5)."""
     if world > 1:
-        n += 2
-    return n
+        return 5
+    return 3 if workload == "decode" else 8
 
 
 def _event_time(torch, fn, reps=20):
@@ -344,37 +342,35 @@ def _event_time(torch, fn, reps=20):
     return a.elapsed_time(b) / reps
 
 
+def payload_ids(torch, rows):
+    """Local expert ids (R, top_k) held in expert-parallel payload rows (w4a8_ep_pack layout)."""
+    o = H + 4 * (H // GROUP) + 4
+    return rows[:, o:o + 4 * TOP_K].contiguous().view(torch.int32)
+
+
 def dominant_kernel(torch, args, world, dist, dev, x, ids, w13, s13, z13, E_total, T, recorded,
                     layer):
-    """The gate_up op on this rank's rows, timed alone with CUDA events on the launching stream.
+    """The step's dominant op on this rank, timed alone with CUDA events on the launching stream.
 
-    decode: the grouped GEMV op (operand quant + w4_stream_kernel + SiLU finish), HBM-bound;
-    algorithmic bytes = touched experts' w13 bytes (codes + scales + zeros) + the fp16
-    activations read + the fp16 SiLU rows written.
+    decode: the whole decode layer op (routing sort + token quant, gate_up GEMV with SiLU, down
+    GEMV with the slot-order reduce: three launches) on the prepacked weights, HBM-bound;
+    algorithmic bytes = touched experts x 1,634,304 B (codes + scales + zeros of w13 and w2)
+    + the fp16 activations read and written. At N > 1 the op is ep_moe_rows on this rank's
+    received rows plus its shared-expert rows.
     prefill: the tcgen05 tile op (tc_quant_rows_kernel, which quantises into sorted order, +
     w4_tc_kernel with the fused SiLU epilogue), tensor-bound; algorithmic FLOPs = 2 * routed rows * 2*inter * hidden
     (padding rows not counted); peak = the dense e4m3 rate, twice the measured bf16 GEMM rate."""
     hbm, fp8_peak, src = peaks()
     import w4a8_fp8_wmma as w4
-    if world > 1:
-        xr = recorded["rows"]
-        idr = recorded["ids"].view(-1, 1).to(torch.int32)
-        idr = torch.where(idr >= 0, idr, torch.full_like(idr, w13.size(0)))
-        E_use, xx, ii = w13.size(0), xr, idr
-    else:
-        E_use, xx, ii = E_total, x, ids
     prefill = args.workload == "prefill" and world == 1
-    block_m, kern = (128, 6) if prefill else (8, 7)
-    s, e, n = w4.moe_align_block_size(ii, block_m, E_use)
-
-    def launch():
-        return torch.ops.w4a8_b200.moe_gemm1_silu(xx, w13, s13, z13, s, e, n, ii.size(1),
-                                                  block_m, kern, False)
-    ms = _max_over_ranks(torch, dist, world, dev, _event_time(torch, launch))
-    valid = ii[(ii >= 0) & (ii < E_use)]
-    touched = int(torch.unique(valid).numel())
-    rows = int(valid.numel())
     if prefill:
+        s, e, n = w4.moe_align_block_size(ids, 128, E_total)
+
+        def launch():
+            return torch.ops.w4a8_b200.moe_gemm1_silu(x, w13, s13, z13, s, e, n, ids.size(1),
+                                                      128, 6, False)
+        ms = _max_over_ranks(torch, dist, world, dev, _event_time(torch, launch))
+        rows = int(ids.numel())
         flops = 2.0 * rows * 2 * INTER * H
         ach = flops / (ms / 1e3) / 1e12
         return {"kernel": "gate_up tile op: tc_quant_rows_kernel + w4_tc_kernel (SiLU epilogue)",
@@ -385,15 +381,35 @@ def dominant_kernel(torch, args, world, dist, dev, x, ids, w13, s13, z13, E_tota
                 "traffic": TC_KERNEL_TRAFFIC,
                 "traffic_source": "profiles/w4_tc_kernel_prefill.md (dram read+write of the "
                                   "w4_tc_kernel launch, one ncu capture)"}
-    bytes_ = touched * W13_BYTES + rows * H * 2 + rows * INTER * 2
+    if world > 1:
+        rows = recorded["rows"]
+        R = rows.size(0)
+        pk = layer.pack
+
+        def launch():
+            return torch.ops.w4a8_b200.ep_moe_rows(rows, pk.p13, pk.p2, pk.E, H, INTER, TOP_K)
+        rid = payload_ids(torch, rows)
+        touched = int(torch.unique(rid[rid >= 0]).numel())
+        act = R * H + R * H * 4
+        kern = "ep_moe_rows: decode_prep + gate_up GEMV + down GEMV (payload rows)"
+    else:
+        from w4a8_fp8_wmma.moe_experts import decode_pack_for
+        w2, s2, z2 = layer
+        pk = decode_pack_for(w13, w2, s13, s2, z13, z2)
+
+        def launch():
+            return pk(x, recorded, ids)
+        touched = int(torch.unique(ids).numel())
+        act = 2 * T * H * 2
+        kern = "moe_decode_packed: decode_prep + gate_up GEMV + down GEMV"
+    ms = _max_over_ranks(torch, dist, world, dev, _event_time(torch, launch))
+    bytes_ = touched * EXPERT_BYTES + act
     ach = bytes_ / (ms / 1e3) / 1e9
-    return {"kernel": "gate_up grouped GEMV op: operand_quant + w4_stream_kernel + finish(SiLU)",
-            "bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
-            "frac": round(ach / hbm, 4), "peak_source": src,
+    return {"kernel": kern, "bound": "hbm", "achieved": round(ach, 1), "peak": hbm,
+            "unit": "GB/s", "frac": round(ach / hbm, 4), "peak_source": src,
             "algorithmic_bytes_per_launch": bytes_, "avg_launch_us": round(ms * 1e3, 2),
-            "traffic": STREAM_KERNEL_TRAFFIC if world == 1 else None,
-            "traffic_source": "profiles/w4_stream_kernel_decode.md (dram read+write, one ncu "
-                              "capture of the stream kernel)" if world == 1 else None}
+            "traffic": DECODE_TRAFFIC if world == 1 else None,
+            "traffic_source": DECODE_TRAFFIC_SRC if world == 1 else None}
 
 
 def _graph_time(torch, fn, steps, warmup):
@@ -562,9 +578,10 @@ def ep_report(torch, dist, world, rank, dev, layer, x, ids, tw, wts, shared):
                        "pass": err <= 1e-2}}
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum of the gate_up w4_stream_kernel launch in the
-# committed ncu capture (profiles/w4_stream_kernel_decode.md).
-STREAM_KERNEL_TRAFFIC = 176_702_208 + 6_877_696
+# dram__bytes_read.sum + dram__bytes_write.sum of the three decode-layer launches in the
+# committed ncu launch list (profiles/decode_layer_launches.md); None until captured.
+DECODE_TRAFFIC = None
+DECODE_TRAFFIC_SRC = "profiles/decode_layer_launches.md (dram read+write summed over the three launches)"
 # The same for the prefill gate_up w4_tc_kernel launch (profiles/w4_tc_kernel_prefill.md).
 TC_KERNEL_TRAFFIC = 305_600_512 + 45_892_096
 

@@ -302,6 +302,12 @@ int moe_launch(const char* op, int epi, const void* x, const int32_t* w_packed,
         t.block_m = (int)block_m;
         t.silu = epi == kEpiSilu ? 1 : 0;
         tc_carve(s.tc, P, K, t);
+        if (x_rows < P) {  // gather: quantise each token once (the stream path's scratch)
+            t.tq = s.xq;
+            t.tq_scale = s.scales;
+            t.tq_sum = reinterpret_cast<float*>(s.xsum);
+            t.x_rows = (int)x_rows;
+        }
         return launch_w4_tc(t, st);
     }
     if (x_rows > 0)

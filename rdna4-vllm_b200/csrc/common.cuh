@@ -31,6 +31,18 @@ __device__ __forceinline__ uint16_t f32x2_to_e4m3x2(float lo, float hi) {
     asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
     return r;
 }
+// e4m3 bytes of x0 / s and x1 / s (IEEE quotients, RNE, satfinite), from the product with the
+// reciprocal r = 1 / s: the product is within 2^-23 (relative) of the quotient, so when both
+// ends of [y (1 - 2^-21), y (1 + 2^-21)] round to the same byte, that byte is the quotient's
+// (the rounding is monotonic); otherwise the IEEE divide decides.
+__device__ __forceinline__ uint16_t quant_pair(float x0, float x1, float s, float r) {
+    const float y0 = x0 * r, y1 = x1 * r;
+    const uint16_t lo = f32x2_to_e4m3x2(y0 * (1.f - 0x1p-21f), y1 * (1.f - 0x1p-21f));
+    const uint16_t hi = f32x2_to_e4m3x2(y0 * (1.f + 0x1p-21f), y1 * (1.f + 0x1p-21f));
+    if (lo == hi) return lo;
+    return f32x2_to_e4m3x2(__fdiv_rn(x0, s), __fdiv_rn(x1, s));
+}
+
 // Two e4m3 bytes (lo, hi) -> half2 (lo, hi); exact.
 __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint16_t v) {
     uint32_t r;

@@ -94,6 +94,12 @@ struct TcArgs {
     uint8_t* xs;                // scratch (P_pad, K): sorted-order e4m3 rows (tc_carve)
     float* asc_s;               // scratch (P_pad,): sorted-order activation scales
     float* ssum;                // scratch (K/128, P_pad): sorted-order group sums, group-major
+    // Token-level operand (gather case, x_rows < P): each source row quantised once, then
+    // gathered into sorted order. Null: every sorted row is quantised from x.
+    uint8_t* tq;                // (x_rows, K) e4m3 bytes
+    float* tq_scale;            // (x_rows,)
+    float* tq_sum;              // (x_rows, K/128)
+    int x_rows;
     const int32_t* w;
     const __half* scales;
     const int32_t* zeros;

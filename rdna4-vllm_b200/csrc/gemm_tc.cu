@@ -597,34 +597,15 @@ w4_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmw,
     }
 }
 
-// One warp per sorted row: the row's source activations are quantised per token to e4m3
-// exactly as act_quant_fp8 does (a_scale = max(amax, 4.48e-6) / 448, q = e4m3_rn(x / a_scale),
-// IEEE divides; w4a8_fp8_wmma/test_correctness.py:74-76) and written in sorted order together
-// with the scale and the per-group sums S of the e4m3 values, so the tile kernel reads its token
-// tiles with plain 2D TMA boxes. Rows past the last valid one (up to the tile-rounded count)
-// and rows with a sentinel id are zero-filled. Requires K % 256 == 0.
-__global__ void __launch_bounds__(256) tc_quant_rows_kernel(const TcArgs a, int NT) {
+// One warp quantises one row per token to e4m3 exactly as act_quant_fp8 does (a_scale =
+// max(amax, 4.48e-6) / 448, q = e4m3_rn(x / a_scale) with the IEEE quotient;
+// w4a8_fp8_wmma/test_correctness.py:74-76): bytes in natural order, the per-group sums S of
+// the e4m3 values (sum[g * sum_stride]) and the scale. K % 256 == 0.
+__device__ __forceinline__ void quant_row_nat_warp(const __half* src, int64_t K, uint8_t* dst,
+                                                   float* sum, int64_t sum_stride, float* scale) {
     const int lane = threadIdx.x & 31;
-    const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-    const int P_valid = a.ntp ? min(a.ntp[0], a.P) : a.P;
-    const int64_t rows = (int64_t)(P_valid + NT - 1) / NT * NT;
-    if (r >= rows) return;
-    int src = -1;
-    if (r < P_valid) {
-        const int e = a.expert_ids ? a.expert_ids[r / a.block_m] : 0;
-        const int sid = a.sorted_ids ? a.sorted_ids[r] : (int)r;
-        if (e >= 0 && e < a.E && sid >= 0 && sid < a.num_valid)
-            src = a.src_identity ? (int)r : sid / a.top_k;
-    }
-    uint2* dst = reinterpret_cast<uint2*>(a.xs + r * a.K);
-    const int nch = (int)(a.K / 8);  // 8-element chunks; chunk i belongs to group i / 16
-    if (src < 0) {
-        for (int i = lane; i < nch; i += 32) dst[i] = make_uint2(0u, 0u);
-        for (int g = lane; g < a.G; g += 32) a.ssum[(int64_t)g * a.P_pad + r] = 0.f;
-        if (lane == 0) a.asc_s[r] = 0.f;
-        return;
-    }
-    const uint4* xr = reinterpret_cast<const uint4*>(a.x + (int64_t)src * a.K);
+    const uint4* xr = reinterpret_cast<const uint4*>(src);
+    const int nch = (int)(K / 8);  // 8-element chunks; chunk i belongs to group i / 16
     float amax = 0.f;
     for (int i = lane; i < nch; i += 32) {
         const uint4 v = __ldg(xr + i);
@@ -638,32 +619,76 @@ __global__ void __launch_bounds__(256) tc_quant_rows_kernel(const TcArgs a, int 
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const float s = __fdiv_rn(fmaxf(amax, kAmaxFloor), kE4m3Max);
-    if (lane == 0) a.asc_s[r] = s;
+    const float rcp = __frcp_rn(s);
+    if (lane == 0) *scale = s;
+    uint2* d2 = reinterpret_cast<uint2*>(dst);
     for (int i0 = 0; i0 < nch; i0 += 32) {  // nch % 32 == 0: lanes 0-15 / 16-31 = one group each
         const int i = i0 + lane;
         const uint4 v = __ldg(xr + i);
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
         uint32_t q[2];
-        float sum = 0.f;
+        float acc = 0.f;
 #pragma unroll
         for (int j = 0; j < 4; j += 2) {
-            const __half2 h0 = *reinterpret_cast<const __half2*>(&w[j]);
-            const __half2 h1 = *reinterpret_cast<const __half2*>(&w[j + 1]);
-            const uint16_t p0 = f32x2_to_e4m3x2(__fdiv_rn(__low2float(h0), s),
-                                                __fdiv_rn(__high2float(h0), s));
-            const uint16_t p1 = f32x2_to_e4m3x2(__fdiv_rn(__low2float(h1), s),
-                                                __fdiv_rn(__high2float(h1), s));
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&w[j + 1]));
+            const uint16_t p0 = quant_pair(f0.x, f0.y, s, rcp);
+            const uint16_t p1 = quant_pair(f1.x, f1.y, s, rcp);
             q[j / 2] = (uint32_t)p0 | ((uint32_t)p1 << 16);
             const uint32_t e0 = e4m3x2_to_f16x2(p0), e1 = e4m3x2_to_f16x2(p1);
             const float2 d0 = __half22float2(*reinterpret_cast<const __half2*>(&e0));
             const float2 d1 = __half22float2(*reinterpret_cast<const __half2*>(&e1));
-            sum += (d0.x + d0.y) + (d1.x + d1.y);
+            acc += (d0.x + d0.y) + (d1.x + d1.y);
         }
-        dst[i] = make_uint2(q[0], q[1]);
+        d2[i] = make_uint2(q[0], q[1]);
 #pragma unroll
-        for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if ((lane & 15) == 0) a.ssum[(int64_t)(i / 16) * a.P_pad + r] = sum;
+        for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if ((lane & 15) == 0) sum[(int64_t)(i / 16) * sum_stride] = acc;
     }
+}
+
+// Gather case: every source row once (tokens), into the token-level operand.
+__global__ void __launch_bounds__(256) tc_quant_tokens_kernel(const TcArgs a) {
+    const int64_t t = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (t >= a.x_rows) return;
+    quant_row_nat_warp(a.x + t * a.K, a.K, a.tq + t * a.K, a.tq_sum + t * a.G, 1, a.tq_scale + t);
+}
+
+// One warp per sorted row: writes the row's e4m3 bytes, scale and group sums in sorted order, so
+// the tile kernel reads its token tiles with plain 2D TMA boxes. With a token-level operand the
+// row is a copy of its token's; otherwise the source row is quantised here. Rows past the last
+// valid one (up to the tile-rounded count) and rows with a sentinel id are zero-filled.
+__global__ void __launch_bounds__(256) tc_quant_rows_kernel(const TcArgs a, int NT) {
+    const int lane = threadIdx.x & 31;
+    const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int P_valid = a.ntp ? min(a.ntp[0], a.P) : a.P;
+    const int64_t rows = (int64_t)(P_valid + NT - 1) / NT * NT;
+    if (r >= rows) return;
+    int src = -1;
+    if (r < P_valid) {
+        const int e = a.expert_ids ? a.expert_ids[r / a.block_m] : 0;
+        const int sid = a.sorted_ids ? a.sorted_ids[r] : (int)r;
+        if (e >= 0 && e < a.E && sid >= 0 && sid < a.num_valid)
+            src = a.src_identity ? (int)r : sid / a.top_k;
+    }
+    uint4* dst = reinterpret_cast<uint4*>(a.xs + r * a.K);
+    const int n16 = (int)(a.K / 16);
+    if (src < 0) {
+        for (int i = lane; i < n16; i += 32) dst[i] = make_uint4(0u, 0u, 0u, 0u);
+        for (int g = lane; g < a.G; g += 32) a.ssum[(int64_t)g * a.P_pad + r] = 0.f;
+        if (lane == 0) a.asc_s[r] = 0.f;
+        return;
+    }
+    if (a.tq) {
+        const uint4* srow = reinterpret_cast<const uint4*>(a.tq + (int64_t)src * a.K);
+        for (int i = lane; i < n16; i += 32) dst[i] = srow[i];
+        for (int g = lane; g < a.G; g += 32)
+            a.ssum[(int64_t)g * a.P_pad + r] = a.tq_sum[(int64_t)src * a.G + g];
+        if (lane == 0) a.asc_s[r] = a.tq_scale[src];
+        return;
+    }
+    quant_row_nat_warp(a.x + (int64_t)src * a.K, a.K, a.xs + r * a.K, a.ssum + r, a.P_pad,
+                       a.asc_s + r);
 }
 
 // ---- tensor maps ----
@@ -705,6 +730,10 @@ int sm_count() {
 template <int NT>
 int launch_tc_t(const TcArgs& a, cudaStream_t stream) {
     const int64_t rows_max = (int64_t)(a.P + NT - 1) / NT * NT;
+    if (a.tq && a.x_rows > 0) {
+        tc_quant_tokens_kernel<<<(unsigned)((a.x_rows + 7) / 8), 256, 0, stream>>>(a);
+        if (int rc = launch_status()) return rc;
+    }
     tc_quant_rows_kernel<<<(unsigned)((rows_max + 7) / 8), 256, 0, stream>>>(a, NT);
     if (int rc = launch_status()) return rc;
     CUtensorMap tmw, tmx;
