@@ -48,6 +48,7 @@
 #include "sm100.cuh"
 #include "e4_operand.cuh"
 #include "stream_core.cuh"
+#include "tcgen05.cuh"
 
 namespace w4a8 {
 
@@ -66,7 +67,11 @@ constexpr int kMaxExperts = 4096;
 enum DecMode : int { kGateUp = 0, kDown = 1 };
 
 // Meta word indices.
-enum : int { kMetaActive = 0, kMetaUnit1 = 1, kMetaUnit2 = 2, kMetaErr = 3, kMetaWords = 4 };
+enum : int {
+    kMetaActive = 0, kMetaUnit1 = 1, kMetaUnit2 = 2, kMetaErr = 3,
+    kMetaSync = 4,  // CTAs of the tensor-core down launch that finished their units
+    kMetaWords = 5
+};
 
 struct DecArgs {
     const int32_t* topk_ids;   // row t's slot j at topk_ids[t * ids_stride + j]
@@ -264,6 +269,21 @@ struct DSmem {
     int bad;
 };
 
+#ifdef W4A8_DEC_TRACE
+// Experiment builds only: per CTA (first 8), per stage event (issue, landed, computed), ns.
+constexpr int kTrCtas = 8, kTrStages = 64;
+__device__ unsigned long long g_dec_trace[2][kTrCtas][kTrStages][8];
+#define DEC_TRACE(mode, stage, ev)                                                              \
+    do {                                                                                       \
+        if (blockIdx.x < kTrCtas && (stage) < kTrStages)                                       \
+            g_dec_trace[mode][blockIdx.x][stage][ev] = global_ns();                            \
+    } while (0)
+#else
+#define DEC_TRACE(mode, stage, ev) \
+    do {                           \
+    } while (0)
+#endif
+
 // Smem weight row m (0..127) of unit slice sl -> weight row n of the expert.
 template <int MODE>
 __device__ __forceinline__ int unit_row(const DecArgs& a, int sl, int m) {
@@ -352,18 +372,29 @@ __device__ __forceinline__ void dec_produce(const DecArgs& a, DSmem& sm, const C
 
 // Down-operand quantisation warp: the 512-wide chunk `chunk` of SiLU row p (fp16, written by the
 // gate_up launch) with scale max(amax[p], 4.48e-6) / 448 -> stage row r: e4m3 bytes in GEMV
-// order, group sums S, scale. Lane l handles 8-element units l and l + 32.
-__device__ __forceinline__ void quant_stage_row(const DecArgs& a, DStage& S, int r, int p,
-                                                int chunk) {
+// order, group sums S, scale. Lane l handles 8-element units l and l + 32. The row's data is
+// fetched (fetch_row) before the stage slot is free, so its latency overlaps the wait.
+struct QRow {
+    float amax;
+    uint4 v0, v1;
+};
+__device__ __forceinline__ QRow fetch_row(const DecArgs& a, int p, int chunk) {
     const int lane = threadIdx.x & 31;
-    const float amax = __uint_as_float(__ldcg(reinterpret_cast<const unsigned*>(a.amax) + p));
-    const float s = __fdiv_rn(fmaxf(amax, kAmaxFloor), kE4m3Max);
-    const float rcp = __frcp_rn(s);
     const uint4* src = reinterpret_cast<const uint4*>(a.silu + (int64_t)p * a.I + (int64_t)chunk * 512);
-    const uint4 v0 = __ldcg(src + lane), v1 = __ldcg(src + lane + 32);
+    QRow q;
+    q.amax = __uint_as_float(__ldcg(reinterpret_cast<const unsigned*>(a.amax) + p));
+    q.v0 = __ldcg(src + lane);
+    q.v1 = __ldcg(src + lane + 32);
+    return q;
+}
+template <class Stage>
+__device__ __forceinline__ void quant_stage_row(Stage& S, int r, const QRow& row) {
+    const int lane = threadIdx.x & 31;
+    const float s = __fdiv_rn(fmaxf(row.amax, kAmaxFloor), kE4m3Max);
+    const float rcp = __frcp_rn(s);
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
-        const uint4 v = k ? v1 : v0;
+        const uint4 v = k ? row.v1 : row.v0;
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
         uint32_t q[2];
         float sum = 0.f;
@@ -418,7 +449,7 @@ __device__ __forceinline__ void dec_compute_t(const DStage& S, int r0, int r1, b
     const int lane = threadIdx.x & 31;
     const int c = lane & 3, tok = lane >> 2;
     const int sh0 = (r0 & 7) * 4, sh1 = (r1 & 7) * 4;
-#pragma unroll 2
+#pragma unroll
     for (int j = 0; j < kDSpi; ++j) {
         const uint8_t* wh = &S.wt[j >> 1][0];
         const int u = (j & 1) * 4 + c;
@@ -477,6 +508,54 @@ __device__ __forceinline__ void dec_compute(const DStage& S, int r0, int r1, int
     else dec_compute_t<1>(S, r0, r1, has_z, tot);
 }
 
+// atomicAdd with acquire-release semantics at GPU scope: orders this warp's earlier stores
+// (made visible to it by a __syncwarp) before the count, and the rows counted by other
+// arrivals before this thread's later loads. The warp need not wait for the result.
+__device__ __forceinline__ int atomic_add_acq_rel_gpu(int* p, int v) {
+    int old;
+    asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// out[t, n .. n+7] = sum_{j ascending} w[t, j] * out2[row(t, j), n .. n+7], fp32 multiply then
+// add (the oracle's slot-order reduce); the rows come from L2 (written by other CTAs).
+__device__ __forceinline__ void combine8(const DecArgs& a, int t, int n) {
+    float acc[8] = {};
+    for (int j = 0; j < a.top_k; ++j) {
+        const int pos = __ldg(a.slot_pos + t * a.top_k + j);
+        if (pos < 0) continue;
+        const float w = __ldg(a.topk_w + (int64_t)t * a.ids_stride + j);
+        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(a.out2 + (int64_t)pos * a.H + n));
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[c]));
+            acc[2 * c] = __fadd_rn(acc[2 * c], __fmul_rn(w, f.x));
+            acc[2 * c + 1] = __fadd_rn(acc[2 * c + 1], __fmul_rn(w, f.y));
+        }
+    }
+    if (a.out_f32) {
+        float4* o = reinterpret_cast<float4*>(static_cast<float*>(a.out) + (int64_t)t * a.H + n);
+        o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    } else {
+        uint4 h;
+        uint32_t* hw = reinterpret_cast<uint32_t*>(&h);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const __half2 p = __floats2half2_rn(acc[2 * c], acc[2 * c + 1]);
+            hw[c] = *reinterpret_cast<const uint32_t*>(&p);
+        }
+        *reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + (int64_t)t * a.H + n) = h;
+    }
+}
+
 // out[t, n, n+1] = fp16(sum_{j ascending} w[t, j] * out2[row(t, j), n, n+1]), fp32 multiply
 // then add (the oracle's slot-order reduce); rows are fetched four slots at a time.
 constexpr int kCombMaxK = 16;
@@ -511,6 +590,25 @@ __device__ __forceinline__ void combine_pair(const DecArgs& a, int t, int n) {
     else
         *reinterpret_cast<__half2*>(static_cast<__half*>(a.out) + (int64_t)t * a.H + n) =
             __floats2half2_rn(acc0, acc1);
+}
+
+// The previous pass's arrivals: every lane whose count completed its (token, chunk) has the
+// warp sum that token's slot rows over the chunk's 16 channels.
+__device__ __forceinline__ void resolve_pending(const DecArgs& a, int old, int t, int chunk,
+                                                int ns, int lane) {
+    const bool mine = old >= 0 && old == ns - 1;  // (token t, chunk) completed by this lane
+    unsigned todo = __ballot_sync(0xffffffffu, mine);
+    if (!todo) return;
+    __threadfence();  // the other arrivals' rows (paired with their release)
+    // four (token, chunk) items at a time: lanes 8i .. 8i+7 take the i-th remaining item
+    while (todo) {
+        const unsigned src = __fns(todo, 0, (lane >> 3) + 1);  // 0xffffffff: no such item
+        const int tt = __shfl_sync(0xffffffffu, t, src & 31);
+        const int cc = __shfl_sync(0xffffffffu, chunk, src & 31);
+        if (src < 32) combine_pair(a, tt, cc * 16 + 2 * (lane & 7));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) todo &= todo - 1;
+    }
 }
 
 template <int MODE, bool PACKED>
@@ -548,6 +646,8 @@ decode_gemv_kernel(const DecArgs a, const __grid_constant__ CUtensorMap tmw) {
             const int q = p + lane;
             return (MODE == kGateUp && q < end) ? a.sorted_tok[q] : 0;
         };
+        int n_issued = 0;
+        int n_iss = 0;
         int4 cur = walk.tab(a, blockIdx.x);
         int4 nxt = walk.tab(a, blockIdx.x + G);
         int src_cur = cur.x >= 0 ? src_of(cur.y, cur.z) : 0;
@@ -561,6 +661,8 @@ decode_gemv_kernel(const DecArgs a, const __grid_constant__ CUtensorMap tmw) {
                 for (int ch = 0; ch < nchunk; ++ch) {
                     if (lane == 0) mbar_wait(&sm.empty[st], ph ^ 1, bad);
                     __syncwarp();
+                    if (lane == 0) DEC_TRACE(MODE, n_issued, 0);
+                    ++n_issued;
                     dec_produce<MODE, PACKED>(a, sm, &tmw, (int)st, e, sl, p0, nrows, ch, nchunk,
                                               src);
                     if (++st == kDStages) {
@@ -600,10 +702,19 @@ decode_gemv_kernel(const DecArgs a, const __grid_constant__ CUtensorMap tmw) {
                     const int nrows = min(kDMaxRows, cur.z - p0);
                     for (int ch = 0; ch < nchunk; ++ch, ++stage_no) {
                         if ((stage_no & 1) == qw) {
+                            QRow q0 = fetch_row(a, p0, ch);
+                            QRow q1 = fetch_row(a, p0 + (nrows > 1 ? 1 : 0), ch);
                             if (lane == 0) mbar_wait(&sm.empty[st], ph ^ 1, bad);
                             __syncwarp();
-                            for (int r = 0; r < nrows; ++r)
-                                quant_stage_row(a, sm.st[st], r, p0 + r, ch);
+                            for (int r = 0; r < nrows; r += 2) {
+                                const QRow c0 = q0, c1 = q1;
+                                if (r + 2 < nrows) {  // next pair in flight during this pair
+                                    q0 = fetch_row(a, p0 + r + 2, ch);
+                                    q1 = fetch_row(a, p0 + (r + 3 < nrows ? r + 3 : r + 2), ch);
+                                }
+                                quant_stage_row(sm.st[st], r, c0);
+                                if (r + 1 < nrows) quant_stage_row(sm.st[st], r + 1, c1);
+                            }
                             __syncwarp();
                             if (lane == 0) mbar_arrive(&sm.full[st]);
                         }
@@ -633,9 +744,12 @@ decode_gemv_kernel(const DecArgs a, const __grid_constant__ CUtensorMap tmw) {
             r1 = warp * 16 + 8 + tok;
         }
         float tot[2][4] = {};
+        int pend_old = -1, pend_t = 0, pend_chunk = 0, pend_nslot = 0;  // down: pending arrival
+        int n_done = 0;
         for (;;) {
             mbar_wait(&sm.full[st], ph, bad);
             __syncwarp();
+            if (warp == 0 && lane == 0) DEC_TRACE(MODE, n_done, 1);
             const DMeta& m = sm.meta[st];
             const int e = m.e;
             if (e < 0 || *bad) break;
@@ -644,7 +758,7 @@ decode_gemv_kernel(const DecArgs a, const __grid_constant__ CUtensorMap tmw) {
             const bool last = m.last;
             // epilogue operands, requested before the stage's MMAs so their latency hides there
             float asc_c[2][2] = {};
-            int my_t = 0;  // down: token of row `lane`
+            int my_t = 0, my_ns = 0;  // down: token of row `lane` and its valid slot count
             if (last) {
 #pragma unroll
                 for (int tg = 0; tg < 2; ++tg)
@@ -656,7 +770,10 @@ decode_gemv_kernel(const DecArgs a, const __grid_constant__ CUtensorMap tmw) {
                                                ? __ldg(a.asc + __ldg(a.sorted_tok + p0 + rl) * a.asc_stride)
                                                : sm.st[st].asc[rl];
                     }
-                if (MODE == kDown && lane < nrows) my_t = __ldg(a.sorted_tok + p0 + lane);
+                if (MODE == kDown && lane < nrows) {
+                    my_t = __ldg(a.sorted_tok + p0 + lane);
+                    my_ns = __ldg(a.nslot + my_t);
+                }
             }
             if (m.chunk == 0) {
 #pragma unroll
@@ -664,16 +781,25 @@ decode_gemv_kernel(const DecArgs a, const __grid_constant__ CUtensorMap tmw) {
 #pragma unroll
                     for (int v = 0; v < 4; ++v) tot[tg][v] = 0.f;
             }
+            if (warp == 0 && lane == 0) DEC_TRACE(MODE, n_done, 3);
 #ifndef W4A8_DEC_SKIP_COMPUTE
             dec_compute(sm.st[st], r0, r1, ntg, PACKED || a.zeros != nullptr, tot);
 #endif
             __syncwarp();
+            if (warp == 0 && lane == 0) DEC_TRACE(MODE, n_done, 2);
+            __syncwarp();
             if (lane == 0) mbar_arrive(&sm.empty[st]);
+            if (warp == 0 && lane == 0) DEC_TRACE(MODE, n_done, 2);
+            ++n_done;
             if (++st == kDStages) {
                 st = 0;
                 ph ^= 1;
             }
             if (!last) continue;
+#ifdef W4A8_DEC_SKIP_EPILOGUE
+            if (tot[0][0] == -12345.678f) a.meta[kMetaErr] = 7;  // keeps the MMAs alive
+            continue;
+#endif
             // ---- pass epilogue (warp-local: no barrier with the other warps) ----
             if (MODE == kGateUp) {
                 // SiLU rows (fp16) and their per-row amax for the down operand's scale
@@ -717,25 +843,22 @@ decode_gemv_kernel(const DecArgs a, const __grid_constant__ CUtensorMap tmw) {
                         }
                     }
                 // per (token, 16-channel chunk) arrival of this warp's rows; the last arrival
-                // of a chunk sums the token's slot rows there
+                // of a chunk sums the token's slot rows there. The count's result is consumed
+                // one pass later (or at the end), so the warp does not wait for it here.
                 __syncwarp();
-                bool mine = false;
-                const int chunk16 = sl * 8 + warp;
+                resolve_pending(a, pend_old, pend_t, pend_chunk, pend_nslot, lane);
+                pend_chunk = sl * 8 + warp;
                 if (lane < nrows) {
-                    __threadfence();  // release: the warp's rows (ordered by the syncwarp)
-                    const int old = atomicAdd(&a.tok_done[(int64_t)my_t * (a.H / 16) + chunk16], 1);
-                    mine = old == __ldg(a.nslot + my_t) - 1;
-                }
-                unsigned todo = __ballot_sync(0xffffffffu, mine);
-                if (todo) __threadfence();  // acquire: the other arrivals' rows
-                while (todo) {
-                    const int src_lane = __ffs(todo) - 1;
-                    todo &= todo - 1;
-                    const int t = __shfl_sync(0xffffffffu, my_t, src_lane);
-                    if (lane < 8) combine_pair(a, t, chunk16 * 16 + 2 * lane);
+                    pend_t = my_t;
+                    pend_nslot = my_ns;
+                    pend_old = atomic_add_acq_rel_gpu(
+                        &a.tok_done[(int64_t)my_t * (a.H / 16) + pend_chunk], 1);
+                } else {
+                    pend_old = -1;
                 }
             }
         }
+        if (MODE == kDown) resolve_pending(a, pend_old, pend_t, pend_chunk, pend_nslot, lane);
     }
     __syncthreads();
     if (threadIdx.x == 0 && sm.bad) atomicOr(a.meta + kMetaErr, 2);
@@ -799,9 +922,525 @@ int launch_dec_gemv_t(const DecArgs& a, int units_max, cudaStream_t st) {
     return launch_status();
 }
 
+
+// ---------------------------------------------------------------------------------------
+// The decode GEMV on the 5th-generation tensor cores (prepacked weights).
+//
+// Roles (16 warps): 8 math warps, 1 producer (as above), 1 MMA warp (owns the tensor memory;
+// lane 0 issues), 2 down-operand quantisation warps, 4 epilogue warps. Per stage (128 weight
+// rows x 512 K), in two half-stages of two 128-groups:
+//   - the math warps copy the stage's token rows into four SW128 K-major B tiles (16 rows x
+//     128 K each); per group each thread expands a quarter of its weight row's 128 codes
+//     (thread = weight row = TMEM lane; the quarters are warps w, w + 4, w + 8, w + 12; four
+//     warps per scheduler hide the expansion's latency) to their exact e4m3 values
+//     (codes8_to_e4m3; the prepack stores each word's codes in the operand's byte order) and
+//     stores them to one of three tensor-memory A buffers (tcgen05.st);
+//   - the MMA thread issues per group 4 x tcgen05.mma.kind::f8f6f4 (M 128, N 16, K 32; A from
+//     tensor memory, B from shared memory) into one of four accumulator buffers and commits
+//     per half-stage (and, after the stage's second half, to the stage's empty barrier). On
+//     B200 such an MMA occupies the tensor pipe about 48 cycles whatever N <= 64, so one MMA
+//     per 32 K (not the two a split of the codes would need) keeps it under the HBM rate;
+//   - the math warps fold the accumulators of half-stage hc - 2 (tcgen05.ld) into fp32
+//     registers, tot += scale * (acc - z * S), while the MMAs of hc - 1 and hc run;
+//   - at a pass end the math warps write tot to a shared-memory tile and the epilogue warps
+//     do the global work (SiLU-and-mul, row amax, down rows, combine arrivals), so no math
+//     warp waits on global memory.
+// A gate_up block interleaves gate and up rows (w4a8_stream_pack), so SiLU-and-mul is one
+// shuffle between adjacent lanes; a down block's 16-channel chunks lie inside one warp.
+// ---------------------------------------------------------------------------------------
+constexpr int kTW = 16;                       // math warps
+constexpr int kTQ = kTW / 4;                  // math warps per TMEM lane quarter
+constexpr int kTCodes = 128 / kTQ;            // codes of a 128-group one thread expands
+constexpr int kTTok = 16 / kTQ;               // token columns one thread folds
+constexpr int kTE = 4;                        // epilogue warps
+constexpr int kTThreads = (kTW + 4 + kTE) * 32;  // + producer, MMA, 2 quantisation warps
+constexpr int kTStages = 4;
+constexpr int kTN = 16;                       // token columns per MMA (= kDMaxRows)
+constexpr int kTHalf = kDSpi / 2;             // groups per half-stage
+constexpr int kTABufs = 3;                    // A buffers (half-stages in flight)
+constexpr int kTDBufs = 4;                    // accumulator buffers
+constexpr uint32_t kTmemCols = 512;           // A: 3 x 2 groups x 32 = 192 columns;
+constexpr uint32_t kDCol0 = kTABufs * kTHalf * 32;  // D: 4 x 2 groups x 16 = 128 columns
+static_assert(kDCol0 + kTDBufs * kTHalf * kTN <= kTmemCols, "tensor memory overflow");
+
+struct alignas(1024) TStage {
+    uint8_t wt[2][128 * 128];                 // the packed block: codes, scales, zero points
+    __half sc[128][kDSpi];
+    uint32_t zr[16][kDSpi];
+    uint8_t pad_[34816 - 34048];
+    uint8_t bsw[kDSpi][kTN * 128];            // B tiles per 128-group, SW128 K-major (1024-aligned)
+    uint8_t act[kDMaxRows][kDActStride];      // token rows as copied / quantised (linear)
+    float xs[kDMaxRows][kDSpi];               // S per (row, group)
+    float asc[kDMaxRows];                     // down: activation scale per row
+};
+static_assert(offsetof(TStage, bsw) % 1024 == 0, "B tiles must be 1024-byte aligned");
+
+struct EpMeta {
+    int sl, p0, nrows;
+    float asc[kTN];                           // down: activation scale per row
+};
+
+struct TSmem {
+    TStage st[kTStages];
+    DMeta meta[kTStages];
+    uint64_t full[kTStages];
+    uint64_t empty[kTStages];
+    float ep[2][kTN][128];                    // pass results handed to the epilogue warps
+    EpMeta epm[2];
+    uint64_t afull[kTABufs], dfull[kTDBufs], dempty[kTDBufs], epfull[2], epempty[2];
+    uint32_t tmem_base;
+    int bad;
+};
+
+__device__ __forceinline__ void umma_f8(uint32_t d, uint32_t a_tmem, uint64_t b_desc,
+                                        uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            smem_u32(bar)));
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kTThreads, 1)
+decode_tc_kernel(const DecArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    TSmem& sm = *reinterpret_cast<TSmem*>(smem_raw +
+                                          ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    volatile int* bad = &sm.bad;
+    const int nsl = MODE == kGateUp ? a.I / 64 : a.H / 128;
+    const int n_active = a.meta[kMetaActive];
+    const int units = n_active * nsl;
+    const int nchunk = (int)(a.K / 512);
+    constexpr uint32_t kQuantArrive = MODE == kDown ? 1 : 0;
+    if (threadIdx.x == 0) {
+        sm.bad = 0;
+        for (int s = 0; s < kTStages; ++s) {
+            mbar_init(&sm.full[s], 2 + kQuantArrive);
+            mbar_init(&sm.empty[s], kTW + 1);
+        }
+        for (int s = 0; s < kTABufs; ++s) mbar_init(&sm.afull[s], kTW);
+        for (int s = 0; s < kTDBufs; ++s) {
+            mbar_init(&sm.dfull[s], 1);
+            mbar_init(&sm.dempty[s], kTW);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&sm.epfull[s], kTW);
+            mbar_init(&sm.epempty[s], kTE);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == kTW + 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(&sm.tmem_base)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::);
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::);
+    const uint32_t tmem = sm.tmem_base;
+    const UnitWalk walk{0, units, nsl};
+    const int G = gridDim.x;
+    uint32_t st = 0, ph = 0;
+    if (warp == kTW) {
+        // ---------------- producer: the same stage stream as decode_gemv_kernel ----------------
+        int n_iss = 0;
+        auto src_of = [&](int p, int end) {
+            const int q = p + lane;
+            return (MODE == kGateUp && q < end) ? a.sorted_tok[q] : 0;
+        };
+        int4 cur = walk.tab(a, blockIdx.x);
+        int4 nxt = walk.tab(a, blockIdx.x + G);
+        int src_cur = cur.x >= 0 ? src_of(cur.y, cur.z) : 0;
+        for (int u = blockIdx.x; u < units; u += G) {
+            const int4 nn = walk.tab(a, u + 2 * G);
+            const int src_nxt = nxt.x >= 0 ? src_of(nxt.y, nxt.z) : 0;
+            const int e = cur.x, sl = u % nsl, q0 = cur.y, q1 = cur.z;
+            for (int p0 = q0; p0 < q1; p0 += kDMaxRows) {
+                const int nrows = min(kDMaxRows, q1 - p0);
+                const int src = p0 == q0 ? src_cur : src_of(p0, q1);
+                for (int ch = 0; ch < nchunk; ++ch) {
+                    if (lane == 0) mbar_wait(&sm.empty[st], ph ^ 1, bad);
+                    __syncwarp();
+                    if (lane == 0) DEC_TRACE(MODE, n_iss, 0);
+                    ++n_iss;
+                    DMeta& m = sm.meta[st];
+                    TStage& S = sm.st[st];
+                    if (lane == 0) {
+                        m.e = e;
+                        m.sl = sl;
+                        m.p0 = p0;
+                        m.nrows = nrows;
+                        m.chunk = ch;
+                        m.last = ch == nchunk - 1;
+                        constexpr uint32_t kActBytes = MODE == kGateUp ? kDSpi * 128 + kDSpi * 4 : 0;
+                        mbar_expect_tx(&sm.full[st], kPackBlock + (uint32_t)nrows * kActBytes);
+                        const int64_t blk = ((int64_t)e * nsl + sl) * nchunk + ch;
+                        bulk_load(&S.wt[0][0], a.packed + blk * kPackBlock, kPackBlock, &sm.full[st]);
+                    }
+                    __syncwarp();
+                    if (MODE == kGateUp && lane < nrows) {
+                        bulk_load(&S.act[lane][0],
+                                  a.xe + (int64_t)src * a.xe_stride + (int64_t)ch * kDSpi * 128,
+                                  kDSpi * 128, &sm.full[st]);
+                        bulk_load(&S.xs[lane][0], a.xsum + (int64_t)src * a.xs_stride + ch * kDSpi,
+                                  kDSpi * 4, &sm.full[st]);
+                    }
+                    if (lane == 0) mbar_arrive(&sm.full[st]);
+                    if (++st == kTStages) {
+                        st = 0;
+                        ph ^= 1;
+                    }
+                }
+            }
+            cur = nxt;
+            nxt = nn;
+            src_cur = src_nxt;
+        }
+        if (lane == 0) mbar_wait(&sm.empty[st], ph ^ 1, bad);
+        __syncwarp();
+        if (lane == 0) {
+            sm.meta[st].e = -1;
+            mbar_arrive(&sm.full[st]);
+            mbar_arrive(&sm.full[st]);
+        }
+    } else if (warp == kTW + 1) {
+        // ---------------- MMA issuer: one handshake per half-stage ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc(128, kTN);
+            uint32_t hc = 0;  // half-stages issued
+            uint32_t ab = 0, abph = 0;  // A buffer of half hc and its barrier phase
+            for (int u = blockIdx.x; u < units && !*bad; u += G) {
+                const int4 cur = walk.tab(a, u);
+                for (int p0 = cur.y; p0 < cur.z; p0 += kDMaxRows)
+                    for (int ch = 0; ch < nchunk; ++ch) {
+                        const uint32_t b_base = smem_u32(&sm.st[st].bsw[0][0]);
+                        for (int k = 0; k < 2; ++k, ++hc) {
+                            const uint32_t db = hc % kTDBufs;
+                            mbar_wait(&sm.afull[ab], abph, bad);
+                            mbar_wait(&sm.dempty[db], ((hc / kTDBufs) & 1) ^ 1, bad);
+                            asm volatile("tcgen05.fence::after_thread_sync;" ::);
+#pragma unroll
+                            for (int jj = 0; jj < kTHalf; ++jj) {
+                                const int j = k * kTHalf + jj;
+                                const uint32_t ta = tmem + (ab * kTHalf + jj) * 32;
+                                const uint32_t d = tmem + kDCol0 + (db * kTHalf + jj) * kTN;
+#pragma unroll
+                                for (int kk = 0; kk < 4; ++kk) {
+                                    const uint64_t dd = desc_sw128(b_base + j * (kTN * 128) + kk * 32);
+                                    umma_f8(d, ta + kk * 8, dd, idesc, kk > 0 ? 1u : 0u);
+                                }
+                            }
+                            umma_commit(&sm.dfull[db]);
+                            if (k == 1) umma_commit(&sm.empty[st]);
+                            if (++ab == kTABufs) {
+                                ab = 0;
+                                abph ^= 1;
+                            }
+                        }
+                        if (++st == kTStages) {
+                            st = 0;
+                            ph ^= 1;
+                        }
+                    }
+            }
+        }
+    } else if (warp >= kTW + 4) {
+        // ---------------- epilogue warps ----------------
+        // Warp ew takes weight rows [32 ew, 32 ew + 32) of each pass (lane = row): gate_up
+        // lanes 2c / 2c+1 hold gate / up of one channel; a down warp's rows are two 16-channel
+        // chunks.
+        const int ew = warp - kTW - 4;
+        const int m = ew * 32 + lane;
+        uint32_t eb = 0, ebph = 0;
+        for (int u = blockIdx.x; u < units && !*bad; u += G) {
+            const int4 cur = walk.tab(a, u);
+            for (int p00 = cur.y; p00 < cur.z && !*bad; p00 += kDMaxRows) {
+                if (lane == 0) mbar_wait(&sm.epfull[eb], ebph, bad);
+                __syncwarp();
+                const EpMeta& md = sm.epm[eb];
+                const int sl = md.sl, p0 = md.p0, nrows = md.nrows;
+                if (MODE == kGateUp) {
+                    const float asc_l = lane < nrows
+                        ? __ldg(a.asc + __ldg(a.sorted_tok + p0 + lane) * a.asc_stride) : 0.f;
+                    const int nch = sl * 64 + 16 * ew + (lane >> 1);
+                    for (int t = 0; t < nrows; ++t) {
+                        const float sc = __shfl_sync(0xffffffffu, asc_l, t);
+                        const float mine = sm.ep[eb][t][m];
+                        const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
+                        float mx = 0.f;
+                        if (!(lane & 1)) {
+                            const __half hv = silu_and_mul_half(mine * sc, other * sc);
+                            a.silu[(int64_t)(p0 + t) * a.I + nch] = hv;
+                            mx = fabsf(__half2float(hv));
+                        }
+#pragma unroll
+                        for (int o = 2; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                        if (lane == 0)
+                            atomicMax(reinterpret_cast<unsigned*>(a.amax) + p0 + t, __float_as_uint(mx));
+                    }
+                } else {
+                    // the down rows; the slot-order combine runs after the grid barrier
+                    const int nch = sl * 128 + m;
+                    for (int t = 0; t < nrows; ++t)
+                        a.out2[(int64_t)(p0 + t) * a.H + nch] = __float2half_rn(sm.ep[eb][t][m] * md.asc[t]);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm.epempty[eb]);
+                if (++eb == 2) {
+                    eb = 0;
+                    ebph ^= 1;
+                }
+            }
+        }
+    } else if (warp > kTW + 1) {
+        // ---------------- down: operand quantisation warps ----------------
+        if (MODE == kDown) {
+            const int qw = warp - kTW - 2;
+            int stage_no = 0;
+            for (int u = blockIdx.x; u < units; u += G) {
+                const int4 cur = walk.tab(a, u);
+                for (int p0 = cur.y; p0 < cur.z; p0 += kDMaxRows) {
+                    const int nrows = min(kDMaxRows, cur.z - p0);
+                    for (int ch = 0; ch < nchunk; ++ch, ++stage_no) {
+                        if ((stage_no & 1) == qw) {
+                            QRow q0 = fetch_row(a, p0, ch);
+                            QRow q1 = fetch_row(a, p0 + (nrows > 1 ? 1 : 0), ch);
+                            if (lane == 0) mbar_wait(&sm.empty[st], ph ^ 1, bad);
+                            __syncwarp();
+                            for (int r = 0; r < nrows; r += 2) {
+                                const QRow c0 = q0, c1 = q1;
+                                if (r + 2 < nrows) {
+                                    q0 = fetch_row(a, p0 + r + 2, ch);
+                                    q1 = fetch_row(a, p0 + (r + 3 < nrows ? r + 3 : r + 2), ch);
+                                }
+                                quant_stage_row(sm.st[st], r, c0);
+                                if (r + 1 < nrows) quant_stage_row(sm.st[st], r + 1, c1);
+                            }
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&sm.full[st]);
+                        }
+                        if (++st == kTStages) {
+                            st = 0;
+                            ph ^= 1;
+                        }
+                    }
+                }
+            }
+            if ((stage_no & 1) == qw) {
+                if (lane == 0) mbar_wait(&sm.empty[st], ph ^ 1, bad);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm.full[st]);
+            }
+        }
+    } else {
+        // ---------------- math warps ----------------
+        // Half-stage hc (groups 2k, 2k+1 of a stage): expand into A buffer hc % 3, then fold
+        // half hc - 2 (its MMAs overlapped the expansion of hc - 1 and hc), then hand A over.
+        // A buffer hc % 3 was last read by the MMAs of hc - 3, which the fold of hc - 3 (one
+        // half earlier) already waited for.
+        const int q = warp & 3, h = warp >> 2;             // lane quarter, code/token quarter
+        const int m = q * 32 + lane;                       // weight row = TMEM lane
+        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        const int sh = (m & 7) * 4;
+        float tot[kTTok] = {};
+        uint32_t n = 0;                                    // stages consumed
+        uint32_t eb = 0, ebph = 0;                         // epilogue buffer and its phase
+        // fold half hh (groups 2k, 2k+1 of stage slot `slot`) into tot; after the second half
+        // of a stage, hand a finished pass to the epilogue warps and release the slot
+        auto retire = [&](uint32_t hh) {
+            const uint32_t slot = (hh >> 1) % kTStages;   // stages fill the ring in order
+            const int k = (int)(hh & 1);
+            const TStage& P = sm.st[slot];
+            const uint32_t db = hh % kTDBufs;
+            // token columns [kTTok h, kTTok h + kTTok) hold rows of this pass only below nrows
+            const bool live = kTTok * h < sm.meta[slot].nrows;
+            if (lane == 0) mbar_wait(&sm.dfull[db], (hh / kTDBufs) & 1, bad);
+            __syncwarp();
+            asm volatile("tcgen05.fence::after_thread_sync;" ::);
+            uint32_t v[kTHalf][kTTok];
+            if (live) {
+#pragma unroll
+                for (int jj = 0; jj < kTHalf; ++jj)
+                    tmem_ld4_nowait(tmem + lane_base + kDCol0 + (db * kTHalf + jj) * kTN + kTTok * h, v[jj]);
+                tmem_wait_ld();
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.dempty[db]);
+            if (live) {
+                static_assert(kTHalf == 2, "the fold reads group pairs");
+                const float2 sc = __half22float2(*reinterpret_cast<const __half2*>(&P.sc[m][2 * k]));
+                const uint2 zw = *reinterpret_cast<const uint2*>(&P.zr[m >> 3][2 * k]);
+                const float nz0 = -(float)((zw.x >> sh) & 0xF), nz1 = -(float)((zw.y >> sh) & 0xF);
+#pragma unroll
+                for (int t = 0; t < kTTok; ++t) {
+                    const float2 xs = *reinterpret_cast<const float2*>(&P.xs[kTTok * h + t][2 * k]);
+                    tot[t] = fmaf(sc.x, fmaf(nz0, xs.x, __uint_as_float(v[0][t])), tot[t]);
+                    tot[t] = fmaf(sc.y, fmaf(nz1, xs.y, __uint_as_float(v[1][t])), tot[t]);
+                }
+            }
+            if (k == 0) return;
+            const DMeta& md = sm.meta[slot];
+            if (md.last) {
+                if (lane == 0) mbar_wait(&sm.epempty[eb], ebph ^ 1, bad);
+                __syncwarp();
+                if (live) {
+#pragma unroll
+                    for (int t = 0; t < kTTok; ++t) {
+                        sm.ep[eb][kTTok * h + t][m] = tot[t];
+                        tot[t] = 0.f;
+                    }
+                }
+                if (warp == 0) {
+                    if (lane == 0) {
+                        sm.epm[eb].sl = md.sl;
+                        sm.epm[eb].p0 = md.p0;
+                        sm.epm[eb].nrows = md.nrows;
+                    }
+                    if (MODE == kDown && lane < kTN) sm.epm[eb].asc[lane] = P.asc[lane];
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm.epfull[eb]);
+                if (++eb == 2) {
+                    eb = 0;
+                    ebph ^= 1;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.empty[slot]);
+        };
+        uint32_t hc = 0;                                   // half-stages expanded
+        uint32_t ab = 0;                                   // A buffer of half hc
+        for (;;) {
+            if (lane == 0) mbar_wait(&sm.full[st], ph, bad);
+            __syncwarp();
+            if (warp == 0 && lane == 0) DEC_TRACE(MODE, n, 1);
+            const int e = sm.meta[st].e;
+            if (e < 0 || *bad) break;
+            TStage& S = sm.st[st];
+            // token rows -> SW128 B tiles (16-byte unit u of row r at u ^ (r & 7)); the rows
+            // from nrows on feed accumulator columns no one reads
+            const int nb = sm.meta[st].nrows * (kDSpi * 8);
+            for (int i = threadIdx.x; i < nb; i += kTW * 32) {
+                const int r = i >> 5, v = i & 31, kb = v >> 3, uu = v & 7;
+                *reinterpret_cast<uint4*>(&S.bsw[kb][r * 128 + ((uu ^ (r & 7)) << 4)]) =
+                    *reinterpret_cast<const uint4*>(&S.act[r][v * 16]);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            if (warp == 0 && lane == 0) DEC_TRACE(MODE, n, 4);
+            for (int k = 0; k < 2; ++k, ++hc) {
+#pragma unroll
+                for (int jj = 0; jj < kTHalf; ++jj) {
+                    const int j = k * kTHalf + jj;
+                    // codes [32 h, 32 h + 32) of group j of row m: 16-byte unit h of the group
+                    const uint8_t* wh = &S.wt[j >> 1][0];
+                    const int u0 = (j & 1) * 4 + h;
+                    const uint4 qa = *reinterpret_cast<const uint4*>(wh + m * 128 + ((u0 ^ (m & 7)) << 4));
+                    const uint32_t w[4] = {qa.x, qa.y, qa.z, qa.w};
+                    uint32_t A[8];
+#ifdef W4A8_TC_NO_EXPAND  // experiment builds only: timing without the code expansion
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) A[2 * i] = A[2 * i + 1] = w[i];
+#else
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) codes8_to_e4m3(w[i], A[2 * i], A[2 * i + 1]);
+#endif
+#ifdef W4A8_TC_NO_ST  // experiment builds only: timing without the tensor-memory stores
+                    if (A[0] == 0x12345678u && A[7] == 0x9abcdef0u) sm.bad = 3;
+#else
+                    tmem_st8(tmem + lane_base + (ab * kTHalf + jj) * 32 + 8 * h, A);
+#endif
+                }
+                if (warp == 0 && lane == 0 && k == 0) DEC_TRACE(MODE, n, 5);
+                // the fold of half hc - 2 overlaps the stores' latency
+                if (hc >= 2) retire(hc - 2);
+                if (warp == 0 && lane == 0) DEC_TRACE(MODE, n, 6 + k);
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                asm volatile("tcgen05.fence::before_thread_sync;" ::);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm.afull[ab]);
+                if (++ab == kTABufs) ab = 0;
+                if (warp == 0 && lane == 0 && k == 0) DEC_TRACE(MODE, n, 3);
+            }
+            if (warp == 0 && lane == 0) DEC_TRACE(MODE, n, 2);
+            ++n;
+            if (++st == kTStages) {
+                st = 0;
+                ph ^= 1;
+            }
+        }
+        if (!*bad) {
+            if (hc >= 2) retire(hc - 2);
+            if (hc >= 1) retire(hc - 1);
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::);
+    __syncthreads();
+    if (threadIdx.x == 0 && sm.bad) atomicOr(a.meta + kMetaErr, 2);
+    if (warp == kTW + 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::);
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(kTmemCols));
+    }
+    if (MODE == kDown) {
+        // grid barrier (the launch is cooperative, so every CTA is resident), then the
+        // slot-order combine of all tokens over the whole grid
+        if (threadIdx.x == 0) {
+            __threadfence();
+            atomicAdd(a.meta + kMetaSync, 1);
+            const uint64_t t0 = global_ns();
+            while (ld_acquire_gpu(a.meta + kMetaSync) < (int)gridDim.x) {
+                if (global_ns() - t0 > kWaitLimitNs) {
+                    atomicOr(a.meta + kMetaErr, 4);
+                    sm.bad = 1;
+                    break;
+                }
+                __nanosleep(64);
+            }
+            __threadfence();
+        }
+        __syncthreads();
+        if (sm.bad) return;
+        const int n8 = a.H / 8;
+        const int items = a.T * n8;
+        for (int i = blockIdx.x * kTThreads + threadIdx.x; i < items; i += gridDim.x * kTThreads)
+            combine8(a, i / n8, (i % n8) * 8);
+    }
+}
+
+template <int MODE>
+int launch_dec_tc(const DecArgs& a, int units_max, cudaStream_t st) {
+    static_assert(sizeof(TSmem) + 1024 <= 227 * 1024, "tensor-core decode shared memory");
+    const size_t smem = sizeof(TSmem) + 1024;
+    cudaError_t ce = cudaFuncSetAttribute(decode_tc_kernel<MODE>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (ce != cudaSuccess) return (int)ce;
+    const int grid = std::max(1, std::min(units_max, sm_count_dev()));
+    if (MODE == kDown) {
+        // cooperative: the closing grid barrier needs every CTA resident (one per SM)
+        DecArgs args = a;
+        void* params[] = {&args};
+        ce = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(decode_tc_kernel<MODE>),
+                                         dim3(grid), dim3(kTThreads), params, smem, st);
+        if (ce != cudaSuccess) return (int)ce;
+        return launch_status();
+    }
+    decode_tc_kernel<MODE><<<grid, kTThreads, smem, st>>>(a);
+    return launch_status();
+}
+
 template <int MODE>
 int launch_dec_gemv(const DecArgs& a, int units_max, cudaStream_t st) {
-    return a.packed ? launch_dec_gemv_t<MODE, true>(a, units_max, st)
+    // prepacked weights: the tensor-core kernel; op layout: the mma.sync kernel
+    return a.packed ? launch_dec_tc<MODE>(a, units_max, st)
                     : launch_dec_gemv_t<MODE, false>(a, units_max, st);
 }
 
@@ -809,10 +1448,20 @@ int launch_dec_gemv(const DecArgs& a, int units_max, cudaStream_t st) {
 // Weight prepack for the decode GEMV: op layout -> one contiguous block per (expert, unit
 // slice, 512-wide K chunk), in the exact shared-memory image of a DStage's weight part:
 //   codes  [2 halves][128 rows][8 x 16 B], 16-byte unit u of row m stored at u ^ (m & 7)
-//          (the 128-byte swizzle the compute warps read);
+//          (the 128-byte swizzle the compute warps read); within each 32-bit word the eight
+//          codes are reordered c0 c2 c4 c6 c1 c3 c5 c7 (gemv_nibble_order);
 //   scales [128 rows][4 groups] fp16;  zeros [16 (8-row words)][4 groups] u32 (8 when absent).
-// Row m of a gate_up block is gate row sl*64 + m (m < 64) or up row inter + sl*64 + m - 64.
+// Row m of a gate_up block is gate row sl*64 + m/2 (m even) or the matching up row
+// inter + sl*64 + (m-1)/2 (m odd), so every gate/up pair sits in adjacent TMEM lanes.
 // ---------------------------------------------------------------------------------------
+// Codes c0..c7 of a word (nibble i = c_i) -> nibble order c0 c2 c4 c6 c1 c3 c5 c7, the GEMV
+// byte order of the e4m3 operand rows, so that nibble i expands to operand byte i.
+__device__ __forceinline__ uint32_t gemv_nibble_order(uint32_t w) {
+    const uint32_t ev = w & 0x0F0F0F0Fu, od = (w >> 4) & 0x0F0F0F0Fu;  // c0 c2 c4 c6 / c1 c3 c5 c7
+    const uint32_t e2 = (ev | (ev >> 4)) & 0x00FF00FFu, o2 = (od | (od >> 4)) & 0x00FF00FFu;
+    return ((e2 | (e2 >> 8)) & 0xFFFFu) | (((o2 | (o2 >> 8)) & 0xFFFFu) << 16);
+}
+
 __global__ void __launch_bounds__(256)
 stream_pack_kernel(const int32_t* __restrict__ w, const __half* __restrict__ scales,
                    const int32_t* __restrict__ zeros, int64_t K, int N, int G, int inter,
@@ -823,15 +1472,19 @@ stream_pack_kernel(const int32_t* __restrict__ w, const __half* __restrict__ sca
     const int64_t e = blk / ((int64_t)nch * nsl);
     uint8_t* dst = packed + blk * kPackBlock;
     const uint8_t* wb = reinterpret_cast<const uint8_t*>(w);
-    auto row_of = [&](int m) {
-        if (inter > 0) return m < 64 ? sl * 64 + m : inter + sl * 64 + (m - 64);
+    auto row_of = [&](int m) {  // gate_up: gate row 64 sl + m/2 (m even), its up row (m odd)
+        if (inter > 0) return (m & 1) ? inter + sl * 64 + (m >> 1) : sl * 64 + (m >> 1);
         return sl * 128 + m;
     };
     for (int idx = threadIdx.x; idx < 2048; idx += blockDim.x) {
         const int h = idx >> 10, m = (idx >> 3) & 127, u = idx & 7;
         const int n = row_of(m);
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(
+        uint4 v = __ldg(reinterpret_cast<const uint4*>(
             wb + ((int64_t)e * N + n) * (K / 2) + (int64_t)ch * 256 + h * 128 + u * 16));
+        v.x = gemv_nibble_order(v.x);
+        v.y = gemv_nibble_order(v.y);
+        v.z = gemv_nibble_order(v.z);
+        v.w = gemv_nibble_order(v.w);
         *reinterpret_cast<uint4*>(dst + h * 16384 + m * 128 + ((u ^ (m & 7)) << 4)) = v;
     }
     if (threadIdx.x < 128) {
@@ -839,11 +1492,23 @@ stream_pack_kernel(const int32_t* __restrict__ w, const __half* __restrict__ sca
         const uint2 v = *reinterpret_cast<const uint2*>(scales + ((int64_t)e * N + n) * G + ch * 4);
         *reinterpret_cast<uint2*>(dst + 32768 + m * 8) = v;
     } else if (threadIdx.x < 144) {
-        const int m8 = threadIdx.x - 128, n8 = row_of(m8 * 8) >> 3;
-        uint4 v = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
-        if (zeros)
-            v = *reinterpret_cast<const uint4*>(zeros + ((int64_t)e * (N / 8) + n8) * G + ch * 4);
-        *reinterpret_cast<uint4*>(dst + 32768 + 1024 + m8 * 16) = v;
+        // zero points of block rows 8 m8 .. 8 m8 + 7, nibble (m % 8), 4 groups
+        const int m8 = threadIdx.x - 128;
+        uint32_t zw[4] = {0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u};
+        if (zeros) {
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+                uint32_t v = 0;
+                for (int i = 0; i < 8; ++i) {
+                    const int n = row_of(m8 * 8 + i);
+                    const uint32_t zz =
+                        (uint32_t)(zeros[((int64_t)e * (N / 8) + (n >> 3)) * G + ch * 4 + g] >> ((n & 7) * 4)) & 0xF;
+                    v |= zz << (4 * i);
+                }
+                zw[g] = v;
+            }
+        }
+        *reinterpret_cast<uint4*>(dst + 32768 + 1024 + m8 * 16) = make_uint4(zw[0], zw[1], zw[2], zw[3]);
     }
 }
 
@@ -1001,3 +1666,9 @@ int run_fused_decode(const DecInput& in, int64_t T, int64_t top_k, int64_t E,
 }  // namespace
 
 }  // namespace w4a8
+
+#ifdef W4A8_DEC_TRACE
+extern "C" W4A8_API int w4a8_debug_dec_trace(void* host, size_t bytes) {
+    return (int)cudaMemcpyFromSymbol(host, w4a8::g_dec_trace, bytes);
+}
+#endif

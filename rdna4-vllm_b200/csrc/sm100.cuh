@@ -40,21 +40,32 @@ __device__ __forceinline__ uint64_t global_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-// Bounded wait: try_wait in a loop (the instruction itself suspends the thread for a short,
-// hardware-defined time), giving up after kWaitLimitNs; once any wait in the CTA has given up,
-// later waits return at once.
+// try_wait that may suspend the thread in hardware for up to hint_ns (it resumes as soon as
+// the phase completes), so a waiting warp does not spin on the issue slots its neighbours need.
+__device__ __forceinline__ bool mbar_try_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return done != 0;
+}
+
+// Bounded wait: a plain try_wait first, then suspending try_waits (up to 20 us each), giving up
+// after kWaitLimitNs; once any wait in the CTA has given up, later waits return at once.
 __device__ __forceinline__ void mbar_wait(uint64_t* bar, uint32_t parity, volatile int* bad) {
     if (mbar_try(bar, parity)) return;
     if (*bad) return;
     const uint64_t t0 = global_ns();
-    for (uint32_t i = 1;; ++i) {
-        if (mbar_try(bar, parity)) return;
-        if ((i & 255) == 0) {
-            if (*bad) return;
-            if (global_ns() - t0 > kWaitLimitNs) {
-                *bad = 1;
-                return;
-            }
+    for (;;) {
+        if (mbar_try_sleep(bar, parity, 20000u)) return;
+        if (*bad) return;
+        if (global_ns() - t0 > kWaitLimitNs) {
+            *bad = 1;
+            return;
         }
     }
 }

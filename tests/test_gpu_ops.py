@@ -452,8 +452,9 @@ def test_stream_pack_matches_layout_restatement(w4, gate_up, asym):
 
 @pytest.mark.parametrize("T,E,asym", [(1, 64, True), (32, 257, True), (32, 64, False), (96, 64, True)])
 def test_packed_decode_layer_equals_unpacked(w4, T, E, asym):
-    """moe_decode_packed on prepacked weights gives the op-layout moe_decode's output bit for
-    bit (same arithmetic, same order), and is within the bar of the oracle."""
+    """moe_decode_packed on prepacked weights (the tensor-core GEMV) and the op-layout
+    moe_decode (the mma.sync GEMV) both meet the bar against the oracle; they accumulate in a
+    different order, so they agree to fp32/fp16 rounding, not bit for bit."""
     c = I.moe_layer_case(1700 + T + E, T, E, 2048, 512, 8, 128, asym=asym)
     z1 = cu(O.pack_zeros(c["z13"])) if asym else torch.empty(0, dtype=torch.int32, device="cuda")
     z2 = cu(O.pack_zeros(c["z2"])) if asym else torch.empty(0, dtype=torch.int32, device="cuda")
@@ -464,8 +465,8 @@ def test_packed_decode_layer_equals_unpacked(w4, T, E, asym):
     p13 = torch.ops.w4a8_b200.stream_pack(w1, s1, z1, True)
     p2 = torch.ops.w4a8_b200.stream_pack(w2, s2, z2, False)
     yp = torch.ops.w4a8_b200.moe_decode_packed(cu(c["x"]), p13, p2, E, 512, tw, ids)
-    assert torch.equal(y.view(torch.int16), yp.view(torch.int16))
     ref = O.moe_layer(c["x"], O.pack_int4(c["c13"]), c["s13"], O.pack_zeros(c["z13"]) if asym else None,
                       O.pack_int4(c["c2"]), c["s2"], O.pack_zeros(c["z2"]) if asym else None,
                       c["topk_ids"], c["topk_weights"])
     assert max_abs_rel(yp.float().cpu().numpy(), ref) <= MAX_ABS_REL
+    assert max_abs_rel(y.float().cpu().numpy(), ref) <= MAX_ABS_REL

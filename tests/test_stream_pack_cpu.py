@@ -21,15 +21,22 @@ def test_stream_pack_roundtrip():
                 for ch in range(K // 512):
                     blk = p[e, sl, ch]
                     for mm in (0, 5, 63, 64, 100, 127):
-                        n = (sl * 64 + mm if mm < 64 else N // 2 + sl * 64 + mm - 64) if gate_up \
+                        n = ((N // 2 if mm % 2 else 0) + sl * 64 + mm // 2) if gate_up \
                             else sl * 128 + mm
                         for h in range(2):
                             for u in range(8):
                                 got = blk[h * 16384 + mm * 128 + (u ^ (mm % 8)) * 16:][:16]
-                                want = wb[e, n, ch * 256 + h * 128 + u * 16:][:16]
+                                want = O.gemv_nibble_order(
+                                    wb[e, n, ch * 256 + h * 128 + u * 16:][:16])
                                 assert np.array_equal(got, want)
                         sc = blk[32768 + mm * 8:][:8].view(np.float16)
                         assert np.array_equal(sc, s[e, n, ch * 4:ch * 4 + 4])
-                        if mm % 8 == 0:
-                            zz = blk[33792 + (mm // 8) * 16:][:16].view(np.uint32)
-                            assert np.array_equal(zz, z.view(np.uint32)[e, n // 8, ch * 4:ch * 4 + 4])
+                        zz = blk[33792 + (mm // 8) * 16:][:16].view(np.uint32)
+                        nib = (zz >> np.uint32(4 * (mm % 8))) & 0xF
+                        assert np.array_equal(nib, O.unpack_zeros(z, N)[e, n, ch * 4:ch * 4 + 4])
+
+
+def test_gemv_nibble_order():
+    """Word 0x76543210 (code i = i) becomes codes 0 2 4 6 1 3 5 7."""
+    b = np.array([0x76543210], "<u4").view(np.uint8)
+    assert O.gemv_nibble_order(b).view("<u4")[0] == 0x75316420
