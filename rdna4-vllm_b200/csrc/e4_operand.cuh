@@ -47,6 +47,7 @@ static __device__ void quant_row_e4(const __half* src, int K, int64_t row, uint8
         amax = red[0];
     }
     const float s = __fdiv_rn(fmaxf(amax, kAmaxFloor), kE4m3Max);
+    const float rcp = __frcp_rn(s);
     if (tid == 0) scale[row] = s;
     const int G = K / 128;
     for (int i0 = 0; i0 < nch; i0 += n_thr) {  // lanes 0-15 / 16-31 of a warp: one group each
@@ -60,10 +61,8 @@ static __device__ void quant_row_e4(const __half* src, int K, int64_t row, uint8
             for (int j = 0; j < 4; j += 2) {
                 const __half2 h0 = *reinterpret_cast<const __half2*>(&w[j]);
                 const __half2 h1 = *reinterpret_cast<const __half2*>(&w[j + 1]);
-                const uint16_t p0 = f32x2_to_e4m3x2(__fdiv_rn(__low2float(h0), s),
-                                                    __fdiv_rn(__high2float(h0), s));
-                const uint16_t p1 = f32x2_to_e4m3x2(__fdiv_rn(__low2float(h1), s),
-                                                    __fdiv_rn(__high2float(h1), s));
+                const uint16_t p0 = quant_pair(__low2float(h0), __high2float(h0), s, rcp);
+                const uint16_t p1 = quant_pair(__low2float(h1), __high2float(h1), s, rcp);
                 q[j / 2] = (uint32_t)p0 | ((uint32_t)p1 << 16);
                 const uint32_t e0 = e4m3x2_to_f16x2(p0), e1 = e4m3x2_to_f16x2(p1);
                 const float2 d0 = __half22float2(*reinterpret_cast<const __half2*>(&e0));

@@ -6,40 +6,36 @@
 // silu_and_mul -> per-token e4m3 re-quantisation -> down GEMM -> fp16 row, then the fp32
 // topk-weighted sum over the token's slots in slot order.
 //
-//   1. decode_prep_kernel   CTA 0 sorts the valid (token, slot) pairs by expert (stable, no
-//                           block padding) and resets the counters of launches 2-3; CTAs 1..T
+//   1. decode_prep_kernel   CTA 0 groups the valid (token, slot) pairs by expert (no block
+//                           padding) and resets the counters of launches 2-3; CTAs 1..T
 //                           quantise one token row each into the GEMV operand format.
-//   2. decode_gemv_kernel<gate_up>
-//                           work unit = (expert, 64 gate rows + the matching 64 up rows, all of
-//                           K). Every warp's m16 tile holds 8 gate rows and the same 8 up rows,
-//                           so each thread ends with gate and up of the same (row, token) and
-//                           applies SiLU-and-mul in registers. The last unit to finish an expert
-//                           (a per-expert counter) quantises that expert's SiLU rows as the down
-//                           GEMM's operand.
-//   3. decode_gemv_kernel<down>
-//                           work unit = (expert, 128 output channels). Rows are rounded to fp16
-//                           (the oracle's per-slot fp16 store); the last unit to finish a
-//                           (token, 128-channel slice) — a per-(token, slice) counter — sums the
-//                           token's slot rows in slot order (fp32 multiply, then add) and writes
-//                           the fp16 output.
-// The intermediates (SiLU rows, the down operand, the per-slot down rows) are a few hundred KB
-// and stay in L2. The results do not depend on scheduling: every sum has a fixed order.
+//   2. gate_up GEMV         work unit = (expert, 64 gate rows + the matching 64 up rows, all of
+//                           K); SiLU-and-mul in the epilogue, fp16 SiLU rows per slot.
+//   3. down GEMV            work unit = (expert, 128 output channels); fp16 rows per slot, then
+//                           the fp32 topk-weighted sum over each token's slots in slot order.
 //
-// GEMV core (both kernels): persistent, one CTA per SM, 8 compute warps + 1 producer warp. Units
-// are dealt round-robin (heavy experts first); the producer streams each unit's K in 512-wide
-// chunks through a 4-stage shared-memory ring: the 128 weight rows with their scales and zero
-// points (one bulk copy of a prepacked block, or TMA + cp.async from the op layout), the unit's
-// e4m3 activation rows (<= 16 per pass; more rows take more passes) and their group sums by
-// bulk copies. The tensor-core arithmetic is mma.sync m16n8k32 on e4m3 operands (see
-// dec_compute_t), folded per 128-group in fp32 with the group scale, then multiplied by the
-// row's activation scale: the reference oracle's association
-// (w4a8_fp8_wmma/test_correctness.py:113-119) up to fp32 rounding.
+// Two implementations of launches 2-3 share the stage stream (a persistent CTA per SM; units
+// dealt round-robin, heavy experts first; 512-wide K chunks through a shared-memory ring fed by
+// one producer warp; <= 16 activation rows per pass):
+//   - prepacked weights (w4a8_stream_pack): decode_tc_kernel, the 5th-generation tensor cores.
+//     The codes are expanded to exact e4m3 values into tensor memory and multiplied with
+//     tcgen05.mma (kind::f8f6f4, M 128 x N 16 x K 32); the accumulators are folded per 128-group
+//     in fp32 (scale, zero point times the operand's group sum). The down launch is cooperative:
+//     it first quantises every SiLU row once (grid-wide), and after its units a grid barrier
+//     precedes the slot-order combine.
+//   - op-layout weights: decode_gemv_kernel, mma.sync m16n8k32 on e4m3 operands (see
+//     dec_compute_t); its down operand is quantised per stage by two warps and its combine is
+//     done by the last arrival per (token, 16-channel chunk).
+// Both fold in the reference oracle's association (w4a8_fp8_wmma/test_correctness.py:113-119)
+// up to fp32 rounding. The intermediates (SiLU rows, the down operand, the per-slot down rows)
+// are a few hundred KB and stay in L2. No result depends on scheduling: every sum has a fixed
+// order.
 //
-// Every mbarrier wait is bounded (sm100.cuh); a wait that gives up sets bit 1 of the error word
-// and the kernel finishes without waiting further. There are no cross-CTA spin-waits: the
-// last-arriver steps are decided by atomic counters.
+// Every mbarrier wait and the grid barrier are bounded (sm100.cuh); a wait that gives up sets
+// the error word and the kernel finishes without waiting further.
 #include <algorithm>
 #include <cstddef>
+#include <type_traits>
 #include <string>
 
 #include "common.cuh"
@@ -82,6 +78,7 @@ struct DecArgs {
     int64_t xs_stride;         // floats between rows of the group sums (K/128 when dense)
     int64_t asc_stride;        // floats between activation scales (1 when dense)
     int out_f32;               // the layer output is fp32 (else fp16)
+    uint32_t one, m1;          // 1 and 0xffffffff (multipliers of codes8_to_e4m3_fma)
     int32_t* off;              // [E + 1] sorted-row offset of each expert
     int32_t* active;           // [E] experts with rows, heavy (> kDMaxRows rows) first
     int32_t* meta;             // kMeta*
@@ -139,6 +136,18 @@ __device__ __forceinline__ int block_excl_scan(int v, int* red, int* total) {
     return base + inc - v;
 }
 
+#ifdef W4A8_DEC_TRACE
+__device__ unsigned long long g_prep_trace[8];
+#define PREP_MARK(i)                                     \
+    do {                                                 \
+        if (threadIdx.x == 0) g_prep_trace[i] = global_ns(); \
+    } while (0)
+#else
+#define PREP_MARK(i) \
+    do {             \
+    } while (0)
+#endif
+
 __global__ void __launch_bounds__(kPrepThreads) decode_prep_kernel(const DecArgs a) {
     extern __shared__ int prep_smem[];
     __shared__ float red[32];
@@ -152,6 +161,7 @@ __global__ void __launch_bounds__(kPrepThreads) decode_prep_kernel(const DecArgs
                             const_cast<float*>(a.xsum), const_cast<float*>(a.asc), red);
         return;
     }
+    PREP_MARK(0);
     const int E = a.E, S = a.T * a.top_k;
     const int n16 = a.H / 16;
     int* cnt = prep_smem;             // [E]
@@ -161,6 +171,7 @@ __global__ void __launch_bounds__(kPrepThreads) decode_prep_kernel(const DecArgs
     if (tid < kMetaWords) a.meta[tid] = 0;
     for (int i = tid; i < a.T * n16; i += kPrepThreads) a.tok_done[i] = 0;
     for (int i = tid; i < S; i += kPrepThreads) a.amax[i] = 0.f;
+    PREP_MARK(1);
     __syncthreads();
     auto slot_id = [&](int s) { return a.topk_ids[(int64_t)(s / a.top_k) * a.ids_stride + s % a.top_k]; };
     for (int s = tid; s < S; s += kPrepThreads) {
@@ -176,6 +187,7 @@ __global__ void __launch_bounds__(kPrepThreads) decode_prep_kernel(const DecArgs
         a.nslot[t] = n;
         ns[t] = n;
     }
+    PREP_MARK(2);
     __syncthreads();
     // offsets (expert order) and the active list (heavy experts first, then the rest; each part
     // in expert order): each thread owns a contiguous run of experts
@@ -187,10 +199,12 @@ __global__ void __launch_bounds__(kPrepThreads) decode_prep_kernel(const DecArgs
         my_heavy += cnt[e] > kDMaxRows;
         my_light += (cnt[e] > 0 && cnt[e] <= kDMaxRows);
     }
+    PREP_MARK(3);
     int tot_rows, tot_heavy, tot_light;
     int base_rows = block_excl_scan(my_rows, ired, &tot_rows);
     int base_heavy = block_excl_scan(my_heavy, ired, &tot_heavy);
     int base_light = block_excl_scan(my_light, ired, &tot_light) + tot_heavy;
+    PREP_MARK(4);
     for (int e = e0; e < e1; ++e) {
         a.off[e] = base_rows;
         cur[e] = base_rows;
@@ -209,32 +223,22 @@ __global__ void __launch_bounds__(kPrepThreads) decode_prep_kernel(const DecArgs
         a.meta[kMetaActive] = tot_heavy + tot_light;
     }
     __syncthreads();
-    // stable placement: slots in ascending order, warps of a chunk in turn
-    const int lane = tid & 31, warp = tid >> 5;
-    for (int c0 = 0; c0 < S; c0 += kPrepThreads) {
-        const int s = c0 + tid;
-        int e = s < S ? slot_id(s) : -1;
-        if (!(e >= 0 && e < E)) e = -1;
-        if (s < S && e < 0) a.slot_pos[s] = -1;
-        for (int w = 0; w < kPrepThreads / 32; ++w) {
-            if (warp == w) {
-                const unsigned m = __match_any_sync(0xffffffffu, e);
-                const int leader = __ffs(m) - 1;
-                const int rank = __popc(m & ((1u << lane) - 1));
-                int base = 0;
-                if (e >= 0 && lane == leader) base = cur[e];
-                base = __shfl_sync(0xffffffffu, base, leader);
-                if (e >= 0) {
-                    const int p = base + rank;
-                    a.slot_pos[s] = p;
-                    a.sorted_slot[p] = s;
-                    a.sorted_tok[p] = s / a.top_k;
-                    if (lane == leader) cur[e] = base + __popc(m);
-                }
-            }
-            __syncthreads();
+    PREP_MARK(5);
+    // placement: one shared-memory atomic per slot. The order of rows inside an expert's
+    // range does not change any result (each row is its own accumulator column and the combine
+    // reads rows through slot_pos in slot order), so it need not be stable.
+    for (int s = tid; s < S; s += kPrepThreads) {
+        const int e = slot_id(s);
+        if (e >= 0 && e < E) {
+            const int p = atomicAdd(&cur[e], 1);
+            a.slot_pos[s] = p;
+            a.sorted_slot[p] = s;
+            a.sorted_tok[p] = s / a.top_k;
+        } else {
+            a.slot_pos[s] = -1;
         }
     }
+    PREP_MARK(6);
     // tokens without a valid slot: the layer output is zero
     for (int t = 0; t < a.T; ++t)
         if (ns[t] == 0)
@@ -242,6 +246,7 @@ __global__ void __launch_bounds__(kPrepThreads) decode_prep_kernel(const DecArgs
                 if (a.out_f32) static_cast<float*>(a.out)[(int64_t)t * a.H + n] = 0.f;
                 else static_cast<__half*>(a.out)[(int64_t)t * a.H + n] = __float2half_rn(0.f);
             }
+    PREP_MARK(7);
 }
 
 // The first three members are one packed weight block (w4a8_stream_pack): a stage of packed
@@ -272,7 +277,7 @@ struct DSmem {
 #ifdef W4A8_DEC_TRACE
 // Experiment builds only: per CTA (first 8), per stage event (issue, landed, computed), ns.
 constexpr int kTrCtas = 8, kTrStages = 64;
-__device__ unsigned long long g_dec_trace[2][kTrCtas][kTrStages][8];
+__device__ unsigned long long g_dec_trace[2][kTrCtas][kTrStages][12];
 #define DEC_TRACE(mode, stage, ev)                                                              \
     do {                                                                                       \
         if (blockIdx.x < kTrCtas && (stage) < kTrStages)                                       \
@@ -527,17 +532,30 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
 // add (the oracle's slot-order reduce); the rows come from L2 (written by other CTAs).
 __device__ __forceinline__ void combine8(const DecArgs& a, int t, int n) {
     float acc[8] = {};
-    for (int j = 0; j < a.top_k; ++j) {
-        const int pos = __ldg(a.slot_pos + t * a.top_k + j);
-        if (pos < 0) continue;
-        const float w = __ldg(a.topk_w + (int64_t)t * a.ids_stride + j);
-        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(a.out2 + (int64_t)pos * a.H + n));
-        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+    for (int j0 = 0; j0 < a.top_k; j0 += 8) {  // eight slots' rows in flight at once
+        int pos[8];
+        float wt[8];
+        uint4 v[8];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[c]));
-            acc[2 * c] = __fadd_rn(acc[2 * c], __fmul_rn(w, f.x));
-            acc[2 * c + 1] = __fadd_rn(acc[2 * c + 1], __fmul_rn(w, f.y));
+        for (int q = 0; q < 8; ++q) {
+            const bool ok = j0 + q < a.top_k;
+            pos[q] = ok ? __ldg(a.slot_pos + t * a.top_k + j0 + q) : -1;
+            wt[q] = ok ? __ldg(a.topk_w + (int64_t)t * a.ids_stride + j0 + q) : 0.f;
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+            if (pos[q] >= 0)
+                v[q] = __ldcg(reinterpret_cast<const uint4*>(a.out2 + (int64_t)pos[q] * a.H + n));
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            if (pos[q] < 0) continue;
+            const uint32_t u[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[c]));
+                acc[2 * c] = __fadd_rn(acc[2 * c], __fmul_rn(wt[q], f.x));
+                acc[2 * c + 1] = __fadd_rn(acc[2 * c + 1], __fmul_rn(wt[q], f.y));
+            }
         }
     }
     if (a.out_f32) {
@@ -866,7 +884,8 @@ decode_gemv_kernel(const DecArgs a, const __grid_constant__ CUtensorMap tmw) {
 
 struct DecLayout {
     size_t off_off, off_active, off_tab, off_stok, off_meta, off_sorted, off_pos, off_nslot,
-        off_amax, off_tokdone, off_xh1, off_xs1, off_sc1, off_silu, off_out2, total;
+        off_amax, off_tokdone, off_xh1, off_xs1, off_sc1, off_silu, off_out2, off_xh2, off_xs2,
+        off_sc2, total;
 };
 
 DecLayout dec_layout(int64_t T, int64_t top_k, int64_t E, int64_t H, int64_t I) {
@@ -893,6 +912,9 @@ DecLayout dec_layout(int64_t T, int64_t top_k, int64_t E, int64_t H, int64_t I) 
     L.off_sc1 = take((size_t)T * 4);
     L.off_silu = take((size_t)S * I * 2);
     L.off_out2 = take((size_t)S * H * 2);
+    L.off_xh2 = take((size_t)S * I);            // the down operand (tensor-core path)
+    L.off_xs2 = take((size_t)S * (I / 128) * 4);
+    L.off_sc2 = take((size_t)S * 4);
     L.total = o;
     return L;
 }
@@ -951,9 +973,8 @@ int launch_dec_gemv_t(const DecArgs& a, int units_max, cudaStream_t st) {
 constexpr int kTW = 16;                       // math warps
 constexpr int kTQ = kTW / 4;                  // math warps per TMEM lane quarter
 constexpr int kTCodes = 128 / kTQ;            // codes of a 128-group one thread expands
-constexpr int kTTok = 16 / kTQ;               // token columns one thread folds
-constexpr int kTE = 4;                        // epilogue warps
-constexpr int kTThreads = (kTW + 4 + kTE) * 32;  // + producer, MMA, 2 quantisation warps
+constexpr int kTE = 4;                        // fold warps (one per TMEM lane quarter)
+constexpr int kTThreads = (kTW + 2 + kTE) * 32;  // + producer, MMA, fold warps
 constexpr int kTStages = 4;
 constexpr int kTN = 16;                       // token columns per MMA (= kDMaxRows)
 constexpr int kTHalf = kDSpi / 2;             // groups per half-stage
@@ -975,19 +996,12 @@ struct alignas(1024) TStage {
 };
 static_assert(offsetof(TStage, bsw) % 1024 == 0, "B tiles must be 1024-byte aligned");
 
-struct EpMeta {
-    int sl, p0, nrows;
-    float asc[kTN];                           // down: activation scale per row
-};
-
 struct TSmem {
     TStage st[kTStages];
     DMeta meta[kTStages];
     uint64_t full[kTStages];
     uint64_t empty[kTStages];
-    float ep[2][kTN][128];                    // pass results handed to the epilogue warps
-    EpMeta epm[2];
-    uint64_t afull[kTABufs], dfull[kTDBufs], dempty[kTDBufs], epfull[2], epempty[2];
+    uint64_t afull[kTABufs], dfull[kTDBufs], dempty[kTDBufs];
     uint32_t tmem_base;
     int bad;
 };
@@ -1006,6 +1020,30 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
             smem_u32(bar)));
 }
 
+// Grid barrier of a cooperative launch on the counter meta[kMetaSync] (zeroed by the prep
+// launch): each CTA adds one, then waits until it reaches `target` (gridDim.x times the barrier's
+// ordinal). Gives up after kWaitLimitNs, setting the error word and *bad.
+__device__ __forceinline__ void grid_barrier(const DecArgs& a, int target, volatile int* bad) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(a.meta + kMetaSync, 1);
+        const uint64_t t0 = global_ns();
+        while (ld_acquire_gpu(a.meta + kMetaSync) < target) {
+            if (global_ns() - t0 > kWaitLimitNs) {
+                atomicOr(a.meta + kMetaErr, 4);
+                *bad = 1;
+                break;
+            }
+            __nanosleep(64);
+        }
+        __threadfence();
+    }
+    __syncthreads();
+    // the rows other CTAs stored are next read by bulk copies (the async proxy)
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(kTThreads, 1)
 decode_tc_kernel(const DecArgs a) {
@@ -1018,21 +1056,16 @@ decode_tc_kernel(const DecArgs a) {
     const int n_active = a.meta[kMetaActive];
     const int units = n_active * nsl;
     const int nchunk = (int)(a.K / 512);
-    constexpr uint32_t kQuantArrive = MODE == kDown ? 1 : 0;
     if (threadIdx.x == 0) {
         sm.bad = 0;
         for (int s = 0; s < kTStages; ++s) {
-            mbar_init(&sm.full[s], 2 + kQuantArrive);
-            mbar_init(&sm.empty[s], kTW + 1);
+            mbar_init(&sm.full[s], 2);
+            mbar_init(&sm.empty[s], kTE + 1);
         }
         for (int s = 0; s < kTABufs; ++s) mbar_init(&sm.afull[s], kTW);
         for (int s = 0; s < kTDBufs; ++s) {
             mbar_init(&sm.dfull[s], 1);
-            mbar_init(&sm.dempty[s], kTW);
-        }
-        for (int s = 0; s < 2; ++s) {
-            mbar_init(&sm.epfull[s], kTW);
-            mbar_init(&sm.epempty[s], kTE);
+            mbar_init(&sm.dempty[s], kTE);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -1046,6 +1079,16 @@ decode_tc_kernel(const DecArgs a) {
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::);
     const uint32_t tmem = sm.tmem_base;
+    if (MODE == kDown) {
+        // the down operand: every SiLU row quantised once (one warp per row over the grid),
+        // then a grid barrier (the launch is cooperative, so every CTA is resident)
+        const int rows = a.off[a.E];
+        constexpr int kWarps = kTThreads / 32;
+        for (int p = blockIdx.x * kWarps + warp; p < rows; p += gridDim.x * kWarps)
+            quant_row_e4<true>(a.silu + (int64_t)p * a.I, a.I, p, const_cast<uint8_t*>(a.xe),
+                               const_cast<float*>(a.xsum), const_cast<float*>(a.asc), nullptr);
+        grid_barrier(a, (int)gridDim.x, &sm.bad);
+    }
     const UnitWalk walk{0, units, nsl};
     const int G = gridDim.x;
     uint32_t st = 0, ph = 0;
@@ -1054,13 +1097,24 @@ decode_tc_kernel(const DecArgs a) {
         int n_iss = 0;
         auto src_of = [&](int p, int end) {
             const int q = p + lane;
-            return (MODE == kGateUp && q < end) ? a.sorted_tok[q] : 0;
+            return q < end ? (MODE == kGateUp ? a.sorted_tok[q] : q) : 0;
         };
-        int4 cur = walk.tab(a, blockIdx.x);
-        int4 nxt = walk.tab(a, blockIdx.x + G);
+        // units are taken from a grid-wide counter (heavy experts come first in the unit
+        // order), two ahead of the one being streamed
+        int* const ctr = a.meta + (MODE == kGateUp ? kMetaUnit1 : kMetaUnit2);
+        auto grab = [&]() {
+            int v = 0;
+            if (lane == 0) v = atomicAdd(ctr, 1);
+            return __shfl_sync(0xffffffffu, v, 0);
+        };
+        int u = grab();
+        int u_nxt = u < units ? grab() : units;
+        int4 cur = walk.tab(a, u);
+        int4 nxt = walk.tab(a, u_nxt);
         int src_cur = cur.x >= 0 ? src_of(cur.y, cur.z) : 0;
-        for (int u = blockIdx.x; u < units; u += G) {
-            const int4 nn = walk.tab(a, u + 2 * G);
+        while (u < units) {
+            const int u_nn = u_nxt < units ? grab() : units;
+            const int4 nn = walk.tab(a, u_nn);
             const int src_nxt = nxt.x >= 0 ? src_of(nxt.y, nxt.z) : 0;
             const int e = cur.x, sl = u % nsl, q0 = cur.y, q1 = cur.z;
             for (int p0 = q0; p0 < q1; p0 += kDMaxRows) {
@@ -1080,13 +1134,13 @@ decode_tc_kernel(const DecArgs a) {
                         m.nrows = nrows;
                         m.chunk = ch;
                         m.last = ch == nchunk - 1;
-                        constexpr uint32_t kActBytes = MODE == kGateUp ? kDSpi * 128 + kDSpi * 4 : 0;
+                        constexpr uint32_t kActBytes = kDSpi * 128 + kDSpi * 4;
                         mbar_expect_tx(&sm.full[st], kPackBlock + (uint32_t)nrows * kActBytes);
                         const int64_t blk = ((int64_t)e * nsl + sl) * nchunk + ch;
                         bulk_load(&S.wt[0][0], a.packed + blk * kPackBlock, kPackBlock, &sm.full[st]);
                     }
                     __syncwarp();
-                    if (MODE == kGateUp && lane < nrows) {
+                    if (lane < nrows) {
                         bulk_load(&S.act[lane][0],
                                   a.xe + (int64_t)src * a.xe_stride + (int64_t)ch * kDSpi * 128,
                                   kDSpi * 128, &sm.full[st]);
@@ -1100,6 +1154,8 @@ decode_tc_kernel(const DecArgs a) {
                     }
                 }
             }
+            u = u_nxt;
+            u_nxt = u_nn;
             cur = nxt;
             nxt = nn;
             src_cur = src_nxt;
@@ -1117,10 +1173,10 @@ decode_tc_kernel(const DecArgs a) {
             constexpr uint32_t idesc = umma_idesc(128, kTN);
             uint32_t hc = 0;  // half-stages issued
             uint32_t ab = 0, abph = 0;  // A buffer of half hc and its barrier phase
-            for (int u = blockIdx.x; u < units && !*bad; u += G) {
-                const int4 cur = walk.tab(a, u);
-                for (int p0 = cur.y; p0 < cur.z; p0 += kDMaxRows)
-                    for (int ch = 0; ch < nchunk; ++ch) {
+            for (;;) {
+                        // the stage's metadata (the end marker has expert -1)
+                        mbar_wait(&sm.full[st], ph, bad);
+                        if (sm.meta[st].e < 0 || *bad) break;
                         const uint32_t b_base = smem_u32(&sm.st[st].bsw[0][0]);
                         for (int k = 0; k < 2; ++k, ++hc) {
                             const uint32_t db = hc % kTDBufs;
@@ -1149,174 +1205,115 @@ decode_tc_kernel(const DecArgs a) {
                             st = 0;
                             ph ^= 1;
                         }
-                    }
             }
         }
-    } else if (warp >= kTW + 4) {
-        // ---------------- epilogue warps ----------------
-        // Warp ew takes weight rows [32 ew, 32 ew + 32) of each pass (lane = row): gate_up
-        // lanes 2c / 2c+1 hold gate / up of one channel; a down warp's rows are two 16-channel
-        // chunks.
-        const int ew = warp - kTW - 4;
-        const int m = ew * 32 + lane;
-        uint32_t eb = 0, ebph = 0;
-        for (int u = blockIdx.x; u < units && !*bad; u += G) {
-            const int4 cur = walk.tab(a, u);
-            for (int p00 = cur.y; p00 < cur.z && !*bad; p00 += kDMaxRows) {
-                if (lane == 0) mbar_wait(&sm.epfull[eb], ebph, bad);
-                __syncwarp();
-                const EpMeta& md = sm.epm[eb];
-                const int sl = md.sl, p0 = md.p0, nrows = md.nrows;
-                if (MODE == kGateUp) {
-                    const float asc_l = lane < nrows
-                        ? __ldg(a.asc + __ldg(a.sorted_tok + p0 + lane) * a.asc_stride) : 0.f;
-                    const int nch = sl * 64 + 16 * ew + (lane >> 1);
-                    for (int t = 0; t < nrows; ++t) {
-                        const float sc = __shfl_sync(0xffffffffu, asc_l, t);
-                        const float mine = sm.ep[eb][t][m];
-                        const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
-                        float mx = 0.f;
-                        if (!(lane & 1)) {
-                            const __half hv = silu_and_mul_half(mine * sc, other * sc);
-                            a.silu[(int64_t)(p0 + t) * a.I + nch] = hv;
-                            mx = fabsf(__half2float(hv));
+    } else if (warp >= kTW + 2) {
+        // ---------------- fold warps ----------------
+        // Warp fw = warp % 4 reads TMEM lane quarter fw: thread = weight row m, all token columns of the
+        // pass. Per half-stage: the accumulators (only the pass's live columns) -> fp32 totals,
+        // tot += scale * (acc - z * S); at a pass end the epilogue (gate_up: lanes 2c / 2c+1
+        // hold gate / up of one channel; down: the fp16 down row of each token).
+        static_assert(kTE == 4, "four consecutive fold warps, one per lane quarter");
+        const int fw = warp & 3;  // a warp reaches TMEM lanes [32 (warp % 4), +32) only
+        const int m = fw * 32 + lane;
+        const uint32_t lane_base = (uint32_t)(fw * 32) << 16;
+        const int sh = (m & 7) * 4;
+        float tot[kTN];
+#pragma unroll
+        for (int t = 0; t < kTN; ++t) tot[t] = 0.f;
+        uint32_t hc = 0;                                   // half-stages folded
+        float asc_l = 0.f;                                 // lane t: the pass's row t scale
+        for (;;) {
+                    const uint32_t stage = hc >> 1;
+                    const uint32_t slot = stage % kTStages;
+                    if (lane == 0) mbar_wait(&sm.full[slot], (stage / kTStages) & 1, bad);
+                    __syncwarp();
+                    const DMeta md = sm.meta[slot];
+                    if (md.e < 0 || *bad) break;
+                    const int sl = md.sl, p0 = md.p0, nrows = md.nrows;
+                    const TStage& P = sm.st[slot];
+                    if (md.chunk == 0) {
+                        // the pass's activation scales, needed only at its end (down: written
+                        // by this launch, so not through the read-only path)
+                        asc_l = lane < nrows
+                            ? __ldcg(a.asc + (int64_t)(MODE == kGateUp ? __ldg(a.sorted_tok + p0 + lane)
+                                                                       : p0 + lane) * a.asc_stride)
+                            : 0.f;
+                    }
+                    for (int k = 0; k < 2; ++k, ++hc) {
+                        const uint32_t db = hc % kTDBufs;
+                        if (lane == 0) mbar_wait(&sm.dfull[db], (hc / kTDBufs) & 1, bad);
+                        __syncwarp();
+                        asm volatile("tcgen05.fence::after_thread_sync;" ::);
+                        uint32_t v[kTHalf][kTN];
+                        const uint32_t d0 = tmem + lane_base + kDCol0 + db * kTHalf * kTN;
+                        if (nrows <= 4) {
+#pragma unroll
+                            for (int jj = 0; jj < kTHalf; ++jj)
+                                tmem_ld4_nowait(d0 + jj * kTN, *reinterpret_cast<uint32_t(*)[4]>(&v[jj][0]));
+                        } else {
+#pragma unroll
+                            for (int jj = 0; jj < kTHalf; ++jj) tmem_ld16_nowait(d0 + jj * kTN, v[jj]);
+                        }
+                        tmem_wait_ld();
+                        asm volatile("tcgen05.fence::before_thread_sync;" ::);
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&sm.dempty[db]);
+                        static_assert(kTHalf == 2, "the fold reads group pairs");
+                        const float2 sc = __half22float2(*reinterpret_cast<const __half2*>(&P.sc[m][2 * k]));
+                        const uint2 zw = *reinterpret_cast<const uint2*>(&P.zr[m >> 3][2 * k]);
+                        const float nz0 = -(float)((zw.x >> sh) & 0xF), nz1 = -(float)((zw.y >> sh) & 0xF);
+                        auto fold = [&](auto ncols) {
+#pragma unroll
+                            for (int t = 0; t < decltype(ncols)::value; ++t) {
+                                const float2 xs = *reinterpret_cast<const float2*>(&P.xs[t][2 * k]);
+                                tot[t] = fmaf(sc.x, fmaf(nz0, xs.x, __uint_as_float(v[0][t])), tot[t]);
+                                tot[t] = fmaf(sc.y, fmaf(nz1, xs.y, __uint_as_float(v[1][t])), tot[t]);
+                            }
+                        };
+                        if (nrows <= 4) fold(std::integral_constant<int, 4>{});
+                        else fold(std::integral_constant<int, kTN>{});
+                    }
+                    if (md.last) {
+                        // the pass epilogue
+                        if (MODE == kGateUp) {
+                            const int nch = sl * 64 + 16 * fw + (lane >> 1);
+#pragma unroll
+                            for (int t = 0; t < kTN; ++t) {
+                                if (t < nrows) {
+                                    const float scl = __shfl_sync(0xffffffffu, asc_l, t);
+                                    const float other = __shfl_xor_sync(0xffffffffu, tot[t], 1);
+                                    if (!(lane & 1))
+                                        a.silu[(int64_t)(p0 + t) * a.I + nch] =
+                                            silu_and_mul_half(tot[t] * scl, other * scl);
+                                }
+                            }
+                        } else {
+                            // the down rows; the slot-order combine runs after the closing
+                            // grid barrier
+                            const int nch = sl * 128 + m;
+#pragma unroll
+                            for (int t = 0; t < kTN; ++t) {
+                                if (t < nrows) {
+                                    const float scl = __shfl_sync(0xffffffffu, asc_l, t);
+                                    a.out2[(int64_t)(p0 + t) * a.H + nch] = __float2half_rn(tot[t] * scl);
+                                }
+                            }
                         }
 #pragma unroll
-                        for (int o = 2; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-                        if (lane == 0)
-                            atomicMax(reinterpret_cast<unsigned*>(a.amax) + p0 + t, __float_as_uint(mx));
+                        for (int t = 0; t < kTN; ++t) tot[t] = 0.f;
                     }
-                } else {
-                    // the down rows; the slot-order combine runs after the grid barrier
-                    const int nch = sl * 128 + m;
-                    for (int t = 0; t < nrows; ++t)
-                        a.out2[(int64_t)(p0 + t) * a.H + nch] = __float2half_rn(sm.ep[eb][t][m] * md.asc[t]);
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&sm.epempty[eb]);
-                if (++eb == 2) {
-                    eb = 0;
-                    ebph ^= 1;
-                }
-            }
-        }
-    } else if (warp > kTW + 1) {
-        // ---------------- down: operand quantisation warps ----------------
-        if (MODE == kDown) {
-            const int qw = warp - kTW - 2;
-            int stage_no = 0;
-            for (int u = blockIdx.x; u < units; u += G) {
-                const int4 cur = walk.tab(a, u);
-                for (int p0 = cur.y; p0 < cur.z; p0 += kDMaxRows) {
-                    const int nrows = min(kDMaxRows, cur.z - p0);
-                    for (int ch = 0; ch < nchunk; ++ch, ++stage_no) {
-                        if ((stage_no & 1) == qw) {
-                            QRow q0 = fetch_row(a, p0, ch);
-                            QRow q1 = fetch_row(a, p0 + (nrows > 1 ? 1 : 0), ch);
-                            if (lane == 0) mbar_wait(&sm.empty[st], ph ^ 1, bad);
-                            __syncwarp();
-                            for (int r = 0; r < nrows; r += 2) {
-                                const QRow c0 = q0, c1 = q1;
-                                if (r + 2 < nrows) {
-                                    q0 = fetch_row(a, p0 + r + 2, ch);
-                                    q1 = fetch_row(a, p0 + (r + 3 < nrows ? r + 3 : r + 2), ch);
-                                }
-                                quant_stage_row(sm.st[st], r, c0);
-                                if (r + 1 < nrows) quant_stage_row(sm.st[st], r + 1, c1);
-                            }
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive(&sm.full[st]);
-                        }
-                        if (++st == kTStages) {
-                            st = 0;
-                            ph ^= 1;
-                        }
-                    }
-                }
-            }
-            if ((stage_no & 1) == qw) {
-                if (lane == 0) mbar_wait(&sm.empty[st], ph ^ 1, bad);
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&sm.full[st]);
-            }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sm.empty[slot]);
         }
     } else {
-        // ---------------- math warps ----------------
-        // Half-stage hc (groups 2k, 2k+1 of a stage): expand into A buffer hc % 3, then fold
-        // half hc - 2 (its MMAs overlapped the expansion of hc - 1 and hc), then hand A over.
-        // A buffer hc % 3 was last read by the MMAs of hc - 3, which the fold of hc - 3 (one
-        // half earlier) already waited for.
-        const int q = warp & 3, h = warp >> 2;             // lane quarter, code/token quarter
+        // ---------------- expansion warps ----------------
+        // Half-stage hc (groups 2k, 2k+1 of a stage) goes to A buffer hc % 3, free once the
+        // MMAs of half hc - 3 completed.
+        const int q = warp & 3, h = warp >> 2;             // lane quarter, code quarter
         const int m = q * 32 + lane;                       // weight row = TMEM lane
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-        const int sh = (m & 7) * 4;
-        float tot[kTTok] = {};
         uint32_t n = 0;                                    // stages consumed
-        uint32_t eb = 0, ebph = 0;                         // epilogue buffer and its phase
-        // fold half hh (groups 2k, 2k+1 of stage slot `slot`) into tot; after the second half
-        // of a stage, hand a finished pass to the epilogue warps and release the slot
-        auto retire = [&](uint32_t hh) {
-            const uint32_t slot = (hh >> 1) % kTStages;   // stages fill the ring in order
-            const int k = (int)(hh & 1);
-            const TStage& P = sm.st[slot];
-            const uint32_t db = hh % kTDBufs;
-            // token columns [kTTok h, kTTok h + kTTok) hold rows of this pass only below nrows
-            const bool live = kTTok * h < sm.meta[slot].nrows;
-            if (lane == 0) mbar_wait(&sm.dfull[db], (hh / kTDBufs) & 1, bad);
-            __syncwarp();
-            asm volatile("tcgen05.fence::after_thread_sync;" ::);
-            uint32_t v[kTHalf][kTTok];
-            if (live) {
-#pragma unroll
-                for (int jj = 0; jj < kTHalf; ++jj)
-                    tmem_ld4_nowait(tmem + lane_base + kDCol0 + (db * kTHalf + jj) * kTN + kTTok * h, v[jj]);
-                tmem_wait_ld();
-            }
-            asm volatile("tcgen05.fence::before_thread_sync;" ::);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.dempty[db]);
-            if (live) {
-                static_assert(kTHalf == 2, "the fold reads group pairs");
-                const float2 sc = __half22float2(*reinterpret_cast<const __half2*>(&P.sc[m][2 * k]));
-                const uint2 zw = *reinterpret_cast<const uint2*>(&P.zr[m >> 3][2 * k]);
-                const float nz0 = -(float)((zw.x >> sh) & 0xF), nz1 = -(float)((zw.y >> sh) & 0xF);
-#pragma unroll
-                for (int t = 0; t < kTTok; ++t) {
-                    const float2 xs = *reinterpret_cast<const float2*>(&P.xs[kTTok * h + t][2 * k]);
-                    tot[t] = fmaf(sc.x, fmaf(nz0, xs.x, __uint_as_float(v[0][t])), tot[t]);
-                    tot[t] = fmaf(sc.y, fmaf(nz1, xs.y, __uint_as_float(v[1][t])), tot[t]);
-                }
-            }
-            if (k == 0) return;
-            const DMeta& md = sm.meta[slot];
-            if (md.last) {
-                if (lane == 0) mbar_wait(&sm.epempty[eb], ebph ^ 1, bad);
-                __syncwarp();
-                if (live) {
-#pragma unroll
-                    for (int t = 0; t < kTTok; ++t) {
-                        sm.ep[eb][kTTok * h + t][m] = tot[t];
-                        tot[t] = 0.f;
-                    }
-                }
-                if (warp == 0) {
-                    if (lane == 0) {
-                        sm.epm[eb].sl = md.sl;
-                        sm.epm[eb].p0 = md.p0;
-                        sm.epm[eb].nrows = md.nrows;
-                    }
-                    if (MODE == kDown && lane < kTN) sm.epm[eb].asc[lane] = P.asc[lane];
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&sm.epfull[eb]);
-                if (++eb == 2) {
-                    eb = 0;
-                    ebph ^= 1;
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.empty[slot]);
-        };
         uint32_t hc = 0;                                   // half-stages expanded
         uint32_t ab = 0;                                   // A buffer of half hc
         for (;;) {
@@ -1328,7 +1325,11 @@ decode_tc_kernel(const DecArgs a) {
             TStage& S = sm.st[st];
             // token rows -> SW128 B tiles (16-byte unit u of row r at u ^ (r & 7)); the rows
             // from nrows on feed accumulator columns no one reads
+#ifdef W4A8_TC_NO_BCOPY  // experiment builds only: timing without the B tile copy
+            const int nb = 0;
+#else
             const int nb = sm.meta[st].nrows * (kDSpi * 8);
+#endif
             for (int i = threadIdx.x; i < nb; i += kTW * 32) {
                 const int r = i >> 5, v = i & 31, kb = v >> 3, uu = v & 7;
                 *reinterpret_cast<uint4*>(&S.bsw[kb][r * 128 + ((uu ^ (r & 7)) << 4)]) =
@@ -1337,6 +1338,12 @@ decode_tc_kernel(const DecArgs a) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             if (warp == 0 && lane == 0) DEC_TRACE(MODE, n, 4);
             for (int k = 0; k < 2; ++k, ++hc) {
+                if (hc >= (uint32_t)kTABufs) {
+                    const uint32_t hp = hc - kTABufs;
+                    if (lane == 0) mbar_wait(&sm.dfull[hp % kTDBufs], (hp / kTDBufs) & 1, bad);
+                    __syncwarp();
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::);
+                }
 #pragma unroll
                 for (int jj = 0; jj < kTHalf; ++jj) {
                     const int j = k * kTHalf + jj;
@@ -1351,18 +1358,11 @@ decode_tc_kernel(const DecArgs a) {
                     for (int i = 0; i < 4; ++i) A[2 * i] = A[2 * i + 1] = w[i];
 #else
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) codes8_to_e4m3(w[i], A[2 * i], A[2 * i + 1]);
+                    for (int i = 0; i < 4; ++i) codes8_to_e4m3_fma(w[i], a.one, a.m1, A[2 * i], A[2 * i + 1]);
 #endif
-#ifdef W4A8_TC_NO_ST  // experiment builds only: timing without the tensor-memory stores
-                    if (A[0] == 0x12345678u && A[7] == 0x9abcdef0u) sm.bad = 3;
-#else
                     tmem_st8(tmem + lane_base + (ab * kTHalf + jj) * 32 + 8 * h, A);
-#endif
                 }
                 if (warp == 0 && lane == 0 && k == 0) DEC_TRACE(MODE, n, 5);
-                // the fold of half hc - 2 overlaps the stores' latency
-                if (hc >= 2) retire(hc - 2);
-                if (warp == 0 && lane == 0) DEC_TRACE(MODE, n, 6 + k);
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 asm volatile("tcgen05.fence::before_thread_sync;" ::);
                 __syncwarp();
@@ -1377,10 +1377,6 @@ decode_tc_kernel(const DecArgs a) {
                 ph ^= 1;
             }
         }
-        if (!*bad) {
-            if (hc >= 2) retire(hc - 2);
-            if (hc >= 1) retire(hc - 1);
-        }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::);
     __syncthreads();
@@ -1390,24 +1386,12 @@ decode_tc_kernel(const DecArgs a) {
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                      "r"(kTmemCols));
     }
+    if (threadIdx.x == 0) DEC_TRACE(MODE, 0, 10);
     if (MODE == kDown) {
         // grid barrier (the launch is cooperative, so every CTA is resident), then the
         // slot-order combine of all tokens over the whole grid
-        if (threadIdx.x == 0) {
-            __threadfence();
-            atomicAdd(a.meta + kMetaSync, 1);
-            const uint64_t t0 = global_ns();
-            while (ld_acquire_gpu(a.meta + kMetaSync) < (int)gridDim.x) {
-                if (global_ns() - t0 > kWaitLimitNs) {
-                    atomicOr(a.meta + kMetaErr, 4);
-                    sm.bad = 1;
-                    break;
-                }
-                __nanosleep(64);
-            }
-            __threadfence();
-        }
-        __syncthreads();
+        grid_barrier(a, 2 * (int)gridDim.x, &sm.bad);
+        if (threadIdx.x == 0) DEC_TRACE(MODE, 0, 11);
         if (sm.bad) return;
         const int n8 = a.H / 8;
         const int items = a.T * n8;
@@ -1611,6 +1595,8 @@ int run_fused_decode(const DecInput& in, int64_t T, int64_t top_k, int64_t E,
     a.out2 = reinterpret_cast<__half*>(ws + L.off_out2);
     a.out = out;
     a.out_f32 = out_f32 ? 1 : 0;
+    a.one = 1u;
+    a.m1 = 0xffffffffu;
     a.x = static_cast<const __half*>(x);
     const int64_t G1 = H / 128;
     if (in.row_bytes == 0) {
@@ -1636,7 +1622,11 @@ int run_fused_decode(const DecInput& in, int64_t T, int64_t top_k, int64_t E,
     if (prep_smem > 48 * 1024)
         cudaFuncSetAttribute(decode_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)prep_smem);
+#ifdef W4A8_PREP_ALIGN_ONLY  // experiment builds only: time the routing sort alone
+    decode_prep_kernel<<<1, kPrepThreads, prep_smem, st>>>(a);
+#else
     decode_prep_kernel<<<(unsigned)(1 + (in.row_bytes ? 0 : T)), kPrepThreads, prep_smem, st>>>(a);
+#endif
     if (int rc = launch_status()) return rc;
     // 2. gate_up GEMV + SiLU (+ the down operand, by each expert's last unit)
     a.packed = static_cast<const uint8_t*>(p13);
@@ -1658,9 +1648,18 @@ int run_fused_decode(const DecInput& in, int64_t T, int64_t top_k, int64_t E,
     a.K = I;
     a.N = (int)H;
     a.G = (int)(I / 128);
-    a.xe = nullptr;  // the down operand is built by the quantisation warps
-    a.xsum = nullptr;
-    a.asc = nullptr;
+    if (p2) {  // the tensor-core down launch quantises each SiLU row once into these
+        a.xe = ws + L.off_xh2;
+        a.xsum = reinterpret_cast<const float*>(ws + L.off_xs2);
+        a.asc = reinterpret_cast<const float*>(ws + L.off_sc2);
+        a.xe_stride = I;
+        a.xs_stride = I / 128;
+        a.asc_stride = 1;
+    } else {  // the mma.sync down launch's quantisation warps build it per stage
+        a.xe = nullptr;
+        a.xsum = nullptr;
+        a.asc = nullptr;
+    }
     return launch_dec_gemv<kDown>(a, (int)std::min<int64_t>(max_active * (H / 128), 1 << 30), st);
 }
 }  // namespace
@@ -1670,5 +1669,13 @@ int run_fused_decode(const DecInput& in, int64_t T, int64_t top_k, int64_t E,
 #ifdef W4A8_DEC_TRACE
 extern "C" W4A8_API int w4a8_debug_dec_trace(void* host, size_t bytes) {
     return (int)cudaMemcpyFromSymbol(host, w4a8::g_dec_trace, bytes);
+}
+#ifdef W4A8_WAIT_COUNT
+extern "C" W4A8_API int w4a8_debug_wait_iters(void* host) {
+    return (int)cudaMemcpyFromSymbol(host, w4a8::g_wait_iters, sizeof(w4a8::g_wait_iters));
+}
+#endif
+extern "C" W4A8_API int w4a8_debug_prep_trace(void* host) {
+    return (int)cudaMemcpyFromSymbol(host, w4a8::g_prep_trace, sizeof(w4a8::g_prep_trace));
 }
 #endif

@@ -37,6 +37,30 @@ static __device__ __forceinline__ void codes8_to_e4m3(uint32_t w, uint32_t& lo, 
     hi = prmt(kLo0, kLo1, w >> 16) | prmt(kHi0, kHi1, wx >> 16);
 }
 
+// Integer multiply-add; with operands the compiler cannot see it issues on the FMA pipe, which
+// the expansion below uses to take work off the integer (ALU) pipe.
+static __device__ __forceinline__ uint32_t imad(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// codes8_to_e4m3 with half of its integer work on the FMA pipe. `one` = 1 and `m1` = 0xffffffff
+// come from kernel arguments (opaque to the compiler). The second lookup takes the complemented
+// selector ~w = w * m1 + m1: a code q >= 8 becomes 15 - q < 8 and selects e4m3(q) from a
+// reversed table; q < 8 becomes >= 8, the sign-replicate mode, giving 0x00. The two lookups'
+// nonzero bytes are disjoint, so their OR is the sum x * one + y.
+static __device__ __forceinline__ void codes8_to_e4m3_fma(uint32_t w, uint32_t one, uint32_t m1,
+                                                          uint32_t& lo, uint32_t& hi) {
+    constexpr uint32_t kLo0 = 0x44403800u, kLo1 = 0x4E4C4A48u;  // e4m3(0..7)
+    constexpr uint32_t kRv0 = 0x54555657u, kRv1 = 0x50515253u;  // byte i: e4m3(15 - i)
+    const uint32_t nw = imad(w, m1, m1);
+    lo = imad(prmt(kLo0, kLo1, w), one, prmt(kRv0, kRv1, nw));
+    const uint32_t wh = w >> 16;
+    const uint32_t nwh = imad(wh, m1, m1);
+    hi = imad(prmt(kLo0, kLo1, wh), one, prmt(kRv0, kRv1, nwh));
+}
+
 // d = a * b + c on two fp32 lanes at once.
 static __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
     uint64_t d;
@@ -108,6 +132,16 @@ static __device__ __forceinline__ void tmem_ld4_nowait(uint32_t taddr, uint32_t 
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
                  : "r"(taddr));
+}
+// 16 consecutive columns of this warp's 32 lanes; the caller waits (tmem_wait_ld).
+static __device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,"
+        "%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+          "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
+          "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
 }
 static __device__ __forceinline__ void tmem_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
