@@ -1100,7 +1100,8 @@ decode_tc_kernel(const DecArgs a) {
             return q < end ? (MODE == kGateUp ? a.sorted_tok[q] : q) : 0;
         };
         // units are taken from a grid-wide counter (heavy experts come first in the unit
-        // order), two ahead of the one being streamed
+        // order). Three are queued: a counter result and a table entry are first used one
+        // unit after they were requested, so a one-stage unit (down) does not wait on them.
         int* const ctr = a.meta + (MODE == kGateUp ? kMetaUnit1 : kMetaUnit2);
         auto grab = [&]() {
             int v = 0;
@@ -1109,11 +1110,14 @@ decode_tc_kernel(const DecArgs a) {
         };
         int u = grab();
         int u_nxt = u < units ? grab() : units;
+        int u_nn = u_nxt < units ? grab() : units;
         int4 cur = walk.tab(a, u);
         int4 nxt = walk.tab(a, u_nxt);
         int src_cur = cur.x >= 0 ? src_of(cur.y, cur.z) : 0;
         while (u < units) {
-            const int u_nn = u_nxt < units ? grab() : units;
+            // lane 0's counter result: shuffled out only in the next iteration
+            int pend = 0;
+            if (lane == 0 && u_nn < units) pend = atomicAdd(ctr, 1);
             const int4 nn = walk.tab(a, u_nn);
             const int src_nxt = nxt.x >= 0 ? src_of(nxt.y, nxt.z) : 0;
             const int e = cur.x, sl = u % nsl, q0 = cur.y, q1 = cur.z;
@@ -1156,6 +1160,7 @@ decode_tc_kernel(const DecArgs a) {
             }
             u = u_nxt;
             u_nxt = u_nn;
+            u_nn = u_nn < units ? __shfl_sync(0xffffffffu, pend, 0) : units;
             cur = nxt;
             nxt = nn;
             src_cur = src_nxt;
