@@ -580,7 +580,7 @@ def ep_report(torch, dist, world, rank, dev, layer, x, ids, tw, wts, shared):
 
 # dram__bytes_read.sum + dram__bytes_write.sum of the three decode-layer launches in the
 # committed ncu launch list (profiles/decode_layer_launches.md); None until captured.
-DECODE_TRAFFIC = None
+DECODE_TRAFFIC = 266110208
 DECODE_TRAFFIC_SRC = "profiles/decode_layer_launches.md (dram read+write summed over the three launches)"
 # The same for the prefill gate_up w4_tc_kernel launch (profiles/w4_tc_kernel_prefill.md).
 TC_KERNEL_TRAFFIC = 305_600_512 + 45_892_096
