@@ -184,7 +184,9 @@ def run_ours(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
+        import datetime
+        # a collective that one rank never joins ends the run in two minutes, not NCCL's ten
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     cfg = workload_config(args.workload)
     T = cfg["T"]
     E_total = E_ROUTED + 1
@@ -267,6 +269,8 @@ def run_ours(args):
                           recorded if world > 1 else tw, layer if world > 1 else (w2, s2, z2))
     e2e = end_to_end(torch, dist, args, world, dev, x_np, ids_np, w_np, layer, run_grouped_moe,
                      (w13, s13, z13, w2, s2, z2), E_total)
+    # every rank takes part in the EP report's collectives before the others leave
+    ep = ep_report(torch, dist, world, rank, dev, layer, x, ids, tw, wts, shared) if world > 1 else None
     if rank != 0:
         _leave(dist, world)
     config = base_config(args.workload, world)
@@ -290,8 +294,8 @@ def run_ours(args):
         "e2e": e2e,
         "gpu_launches": args.steps * launches_per_step(args.workload, world),
     }
-    if world > 1:
-        res["ep"] = ep_report(torch, dist, world, rank, dev, layer, x, ids, tw, wts, shared)
+    if ep is not None:
+        res["ep"] = ep
     if world == 1 and args.workload == "decode" and not args.no_extras:
         res["prefill"] = prefill_record(torch, dev, (w13, s13, z13, w2, s2, z2), E_total, args)
         res["dense"] = dense_record(torch, dev, args)
