@@ -204,6 +204,21 @@ W4A8_API int w4a8_silu_and_mul(const void* x, void* out, int64_t M, int64_t inte
                                w4a8_stream_t stream);
 
 /*
+ * MoE router in one launch: logits (num_tokens, num_experts) of dtype 0 = fp32, 1 = fp16,
+ * 2 = bf16 -> topk_ids (num_tokens, top_k) int32 and topk_weights (num_tokens, top_k) fp32:
+ * softmax over the experts (fp32), the top_k largest in descending order (ties: lower expert
+ * index first), divided by their sum when renormalize != 0. expert_counts (num_experts,) int32,
+ * optional (may be null), receives the number of slots routed to each expert (zeroed first).
+ * Replaces the router vLLM runs before the reference's moe_align call
+ * (w4a8_fp8_wmma/w4a8_fp8_wmma/moe_experts.py:587-589 takes its topk_ids / topk_weights).
+ * Limits: num_experts <= 1024, top_k <= 16.
+ */
+W4A8_API int w4a8_route_topk(const void* logits, int32_t logits_dtype, int64_t num_tokens,
+                             int32_t num_experts, int32_t top_k, int32_t renormalize,
+                             int32_t* topk_ids, float* topk_weights, int32_t* expert_counts,
+                             w4a8_stream_t stream);
+
+/*
  * Expert-parallel dispatch (no counterpart in the reference, which has no expert parallelism;
  * its expert_map is only forwarded to vLLM's align, w4a8_fp8_wmma/w4a8_fp8_wmma/
  * moe_experts.py:587-589). Each of the T tokens is quantised once (the oracle's per-token e4m3

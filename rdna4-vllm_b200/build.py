@@ -25,7 +25,7 @@ CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 
 CU_SOURCES = ["act_quant.cu", "moe_align.cu", "gemm_mma.cu", "gemv_stream.cu", "gemm_tc.cu", "reduce.cu", "moe_layer.cu", "moe_decode.cu", "ep_dispatch.cu",
-              "capi.cu"]
+              "router.cu", "capi.cu"]
 LIB = os.path.join(PKG, "libw4a8_b200.so")
 SHIM = os.path.join(PKG, "_C.so")
 

@@ -262,6 +262,26 @@ std::vector<at::Tensor> act_quant_fp8_forward(const at::Tensor& x) {
     return {q, s};
 }
 
+std::vector<at::Tensor> route_topk_forward(const at::Tensor& logits, int64_t top_k,
+                                           bool renormalize) {
+    TORCH_CHECK(logits.is_cuda() && logits.dim() == 2 && logits.is_contiguous(),
+                "logits must be a contiguous (T, E) CUDA tensor");
+    int32_t dt;
+    if (logits.scalar_type() == at::kFloat) dt = 0;
+    else if (logits.scalar_type() == at::kHalf) dt = 1;
+    else if (logits.scalar_type() == at::kBFloat16) dt = 2;
+    else TORCH_CHECK(false, "logits must be fp32, fp16 or bf16");
+    const c10::cuda::CUDAGuard guard(logits.device());
+    auto ids = at::empty({logits.size(0), top_k}, logits.options().dtype(at::kInt));
+    auto w = at::empty({logits.size(0), top_k}, logits.options().dtype(at::kFloat));
+    auto counts = at::empty({logits.size(1)}, logits.options().dtype(at::kInt));
+    check_status(w4a8_route_topk(logits.data_ptr(), dt, logits.size(0), (int32_t)logits.size(1),
+                                 (int32_t)top_k, renormalize ? 1 : 0, ids.data_ptr<int32_t>(),
+                                 w.data_ptr<float>(), counts.data_ptr<int32_t>(), cur_stream()),
+                 "route_topk");
+    return {ids, w, counts};
+}
+
 std::vector<at::Tensor> moe_align_block_size_forward(const at::Tensor& topk_ids, int64_t block_m,
                                                      int64_t num_experts,
                                                      const c10::optional<at::Tensor>& expert_map,
@@ -511,6 +531,7 @@ TORCH_LIBRARY_IMPL(w4a8_fp8_wmma, CUDA, m) {
 TORCH_LIBRARY(w4a8_b200, m) {
     m.def("act_quant_fp8(Tensor x) -> Tensor[]");
     m.def("silu_and_mul(Tensor x) -> Tensor");
+    m.def("route_topk(Tensor logits, int top_k, bool renormalize) -> Tensor[]");
     m.def("ep_pack(Tensor x, Tensor topk_ids, Tensor topk_weights, int experts_per_rank, int world, "
           "int shared_local_id) -> Tensor[]");
     m.def("ep_moe_rows(Tensor rows, Tensor p13, Tensor p2, int num_experts, int hidden, int inter, "
@@ -533,6 +554,7 @@ TORCH_LIBRARY(w4a8_b200, m) {
 TORCH_LIBRARY_IMPL(w4a8_b200, CUDA, m) {
     m.impl("act_quant_fp8", &act_quant_fp8_forward);
     m.impl("silu_and_mul", &silu_and_mul_forward);
+    m.impl("route_topk", &route_topk_forward);
     m.impl("ep_pack", &ep_pack_forward);
     m.impl("ep_moe_rows", &ep_moe_rows_forward);
     m.impl("ep_gather", &ep_gather_forward);

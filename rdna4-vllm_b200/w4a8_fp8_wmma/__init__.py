@@ -165,6 +165,16 @@ def silu_and_mul(x: torch.Tensor) -> torch.Tensor:
     return torch.ops.w4a8_b200.silu_and_mul(x.contiguous())
 
 
+def route_topk(logits: torch.Tensor, top_k: int, renormalize: bool = True):
+    """The MoE router in one launch: (T, E) fp32/fp16/bf16 logits -> topk_ids (T, top_k) int32,
+    topk_weights (T, top_k) fp32 (softmax, the top_k largest with ties to the lower expert,
+    renormalised) and expert_counts (E,) int32, the slots routed to each expert. It produces the
+    inputs vLLM's router hands to the reference's moe_align call (moe_experts.py:587-589)."""
+    ids, w, counts = torch.ops.w4a8_b200.route_topk(logits.contiguous(), int(top_k),
+                                                    bool(renormalize))
+    return ids, w, counts
+
+
 # ---- Fake / meta impls (output contracts of the CUDA impls, reference __init__.py:240-297) ----
 _register_fake = getattr(getattr(torch, "library", None), "register_fake", None)
 if _register_fake is not None:
@@ -202,6 +212,13 @@ if _register_fake is not None:
                                        expert_ids, num_tokens_post_padded, topk_weights, output,
                                        top_k, block_m, kernel, weight_is_e2m1=False):
         return None
+
+    @_register_fake("w4a8_b200::route_topk")
+    def _fake_route_topk(logits, top_k, renormalize):
+        T, E = logits.shape
+        return [logits.new_empty((T, top_k), dtype=torch.int32),
+                logits.new_empty((T, top_k), dtype=torch.float32),
+                logits.new_empty((E,), dtype=torch.int32)]
 
     @_register_fake("w4a8_b200::silu_and_mul")
     def _fake_silu_and_mul(x):
