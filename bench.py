@@ -447,6 +447,108 @@ def dominant_kernel(torch, args, world, dist, dev, x, ids, w13, s13, z13, E_tota
             "traffic_source": DECODE_TRAFFIC_SRC if world == 1 else None}
 
 
+def run_stack(args):
+    """a 40-layer MoE stack, expert parallel over the ranks of this node (256
+    experts split evenly, the shared expert replicated), independently seeded weights per layer.
+    Decode: 256 tokens in total (256/N per rank) through all layers, one CUDA graph per step.
+    Prefill: a separate 16384-token batch (16384/N per rank), eager (its exchange sizes rows on
+    the host). Each layer is applied to the step's input (the stack's work and traffic per layer
+    without a residual stream). Rank 0 prints one JSON line; time is the max over ranks.
+    Prefill parity: layer 0 on each rank's tokens against the single-GPU composition with the
+    all-gathered weights (max-abs-rel, max over ranks)."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import w4a8_fp8_wmma as w4  # noqa: F401
+    from w4a8_fp8_wmma.ep import ExpertParallelMoE
+    from w4a8_fp8_wmma.moe_experts import run_grouped_moe
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29533")
+    os.environ.setdefault("RANK", "0")
+    os.environ.setdefault("WORLD_SIZE", "1")
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    L = args.layers
+    E_loc = E_ROUTED // world
+    layers = []
+    for l in range(L):
+        w13, s13, z13, w2, s2, z2 = make_layer(torch, dev, 100000 + 1000 * l + rank, E_loc)
+        shared = make_layer(torch, dev, 900000 + l, 1)
+        layers.append(ExpertParallelMoE(w13, s13, z13, w2, s2, z2, E_ROUTED, TOP_K,
+                                        shared=shared))
+
+    def tokens(T, zipf, seed):
+        x_np, ids_np, w_np = make_tokens(T, zipf, seed)
+        return (torch.from_numpy(x_np).to(dev), torch.from_numpy(ids_np[:, :TOP_K].copy()).to(dev),
+                torch.from_numpy(w_np[:, :TOP_K].copy()).to(dev))
+
+    Td, Tp = 256 // world, 16384 // world
+    xd, idd, twd = tokens(Td, False, 7000 + rank)
+    xp, idp, twp = tokens(Tp, True, 8000 + rank)
+    hold = {}
+
+    def dec_step():
+        for lay in layers:
+            hold["d"] = lay(xd, idd, twd)
+
+    def pre_step():
+        for lay in layers:
+            hold["p"] = lay(xp, idp, twp)
+
+    dist.barrier()
+    from w4a8_fp8_wmma.moe_experts import GEMV_MAX_M
+    if Td <= GEMV_MAX_M:
+        ms_d, graphed = _graph_time(torch, dec_step, args.steps, args.warmup)
+    else:  # above the decode split the exchange sizes rows on the host: eager steps
+        ms_d, graphed = _event_time(torch, dec_step, reps=args.steps), False
+    ms_d = _max_over_ranks(torch, dist, world, dev, ms_d)
+    dist.barrier()
+    ms_p = _max_over_ranks(torch, dist, world, dev,
+                           _event_time(torch, pre_step, reps=max(1, min(args.steps, 3))))
+    # prefill parity, layer 0
+    lay = layers[0]
+    y = lay(xp, idp, twp)
+    full = []
+    for t_loc, t_sh in zip(lay.weights, lay.shared):
+        parts = [torch.empty_like(t_loc) for _ in range(world)]
+        dist.all_gather(parts, t_loc.contiguous())
+        full.append(torch.cat(parts + [t_sh], 0).contiguous())
+    w13, s13, z13, w2, s2, z2 = full
+    ids_all = torch.cat([idp, torch.full((Tp, 1), E_ROUTED, dtype=idp.dtype, device=dev)], 1)
+    tw_all = torch.cat([twp, torch.ones((Tp, 1), dtype=twp.dtype, device=dev)], 1)
+    ref = run_grouped_moe(xp, w13, w2, s13, s2, z13, z2, tw_all, ids_all,
+                          global_num_experts=E_ROUTED + 1, out_dtype=torch.float32)
+    err = float((y.float() - ref).abs().max() / ref.abs().max().clamp_min(1e-30))
+    err = _max_over_ranks(torch, dist, world, dev, err)
+    del full, ref
+    if rank == 0:
+        res = {"metric": "40-layer MoE stack tokens/s (configs[4], expert parallel)",
+               "value": round(256 / (ms_d / 1e3), 1), "unit": "tokens/s", "n_gpus": world,
+               "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_d, 4),
+               "higher_is_better": True, "scaling": "strong",
+               "dtype": "e4m3 x int4 -> fp32 (fp16 io)",
+               "data": "synthetic (seeded; independently seeded random-init weights per layer)",
+               "config": {"workload": "configs[4] 40-layer MoE stack, decode 256 tokens",
+                          "layers": L, "tokens_total": 256, "tokens_per_gpu": Td,
+                          "experts": E_ROUTED, "experts_per_gpu": E_loc, "shared_experts": 1,
+                          "top_k": TOP_K, "hidden": H, "inter": INTER,
+                          "parallelism": f"ep{world}",
+                          "graph": "one CUDA graph per step" if graphed else "eager steps",
+                          "layer_input": "each layer applied to the step's input"},
+               "prefill": {"tokens_total": 16384, "tokens_per_gpu": Tp, "routing": "Zipf(1.1)",
+                           "ms_per_step": round(ms_p, 3),
+                           "tokens_per_s": round(16384 / (ms_p / 1e3), 1), "timing": "eager",
+                           "parity_layer0": {"max_abs_rel": err, "pass": err <= 1e-2,
+                                             "vs": "single-GPU run_grouped_moe with the "
+                                                   "all-gathered weights"}}}
+        print(json.dumps(res), flush=True)
+    _leave(dist, world)
+
+
 def _graph_time(torch, fn, steps, warmup):
     """Capture fn in a CUDA graph (eager if capture fails) and time `steps` replays."""
     stream = torch.cuda.Stream()
@@ -775,7 +877,9 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "prefill", "stack"], default="decode",
+                    help="stack: configs[4], the 40-layer expert-parallel stack (run_stack)")
+    ap.add_argument("--layers", type=int, default=40, help="layers of the stack workload")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
@@ -787,8 +891,13 @@ def main():
         args.warmup = 3
     if args.profile_op:
         profile_op(args)
+    elif args.impl == "reference" and args.workload == "stack":
+        print(json.dumps({"impl": "reference", "unavailable": "the reference has no expert "
+                          "parallelism; the stack workload has no reference arm"}), flush=True)
     elif args.impl == "reference":
         run_reference(args)
+    elif args.workload == "stack":
+        run_stack(args)
     else:
         run_ours(args)
 

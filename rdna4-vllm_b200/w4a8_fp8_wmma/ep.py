@@ -16,6 +16,11 @@ Rank r of W owns routed experts [r*E/W, (r+1)*E/W) and its own T tokens.
   3. combine - one all_to_all returns each row to its source; the source sums a token's rows
      over ranks in rank order (fp32) and adds its shared-expert row.
 
+Prefill-size batches (T > GEMV_MAX_M tokens per rank, the same split as run_grouped_moe) send
+fp16 rows with their local ids and weights instead, and the owner runs the reference
+composition (run_grouped_moe: tile GEMMs) on the received rows, with slots owned elsewhere
+mapped to a remote expert through expert_map; the shared expert runs on the rank's own tokens.
+
 Every rank must pass the same token count T (the all_to_all chunk size); the first call with a
 new T checks this across the group and raises on a mismatch. A caller whose ranks hold different
 token counts passes `max_tokens`: each rank's batch is padded to it with empty rows.
@@ -73,7 +78,9 @@ class ExpertParallelMoE:
         self.max_tokens = max_tokens
         self.expert_fn = expert_fn
         self.shared = shared  # (w13, s13, z13, w2, s2, z2) of one replicated shared expert
+        self.weights = (w13, s13, z13, w2, s2, z2)
         self._checked_T: set[int] = set()
+        self._remote_map = None
         self.pack = None
         if expert_fn is None and w13 is not None and w13.is_cuda:
             from .moe_experts import DecodePack
@@ -147,14 +154,46 @@ class ExpertParallelMoE:
         if x.is_cuda and self.expert_fn is None:
             if self.pack is None:
                 raise RuntimeError("ExpertParallelMoE: no CUDA expert weights on this rank")
-            out = self._forward_cuda(x, topk_ids, topk_weights)
+            from .moe_experts import GEMV_MAX_M
+            if x.size(0) > GEMV_MAX_M:
+                out = self._forward_generic(x, topk_ids, topk_weights, self._prefill_experts,
+                                            self._prefill_shared)
+            else:
+                out = self._forward_cuda(x, topk_ids, topk_weights)
         else:
             out = self._forward_generic(x, topk_ids, topk_weights)
         return out[:T_in]
 
-    def _forward_generic(self, x, topk_ids, topk_weights):
-        """The same exchange in plain torch ops (CPU ranks, custom experts)."""
-        if self.expert_fn is None:
+    def _prefill_experts(self, rows, local_ids, w):
+        """The rank's routed experts on received fp16 rows: run_grouped_moe with slots owned
+        elsewhere (-1) sent to a remote expert id E_loc that expert_map drops."""
+        from .moe_experts import run_grouped_moe
+        w13, s13, z13, w2, s2, z2 = self.weights
+        if self._remote_map is None or self._remote_map.device != rows.device:
+            m = torch.arange(self.E_loc + 1, dtype=torch.int32, device=rows.device)
+            m[self.E_loc] = -1
+            self._remote_map = m
+        ids = torch.where(local_ids >= 0, local_ids,
+                          torch.full_like(local_ids, self.E_loc)).to(torch.int32)
+        return run_grouped_moe(rows.to(torch.float16), w13, w2, s13, s2, z13, z2, w, ids,
+                               global_num_experts=self.E_loc + 1, expert_map=self._remote_map,
+                               out_dtype=torch.float32)
+
+    def _prefill_shared(self, x):
+        from .moe_experts import run_grouped_moe
+        w13, s13, z13, w2, s2, z2 = self.shared
+        T = x.size(0)
+        ids = torch.zeros((T, 1), dtype=torch.int32, device=x.device)
+        ones = torch.ones((T, 1), dtype=torch.float32, device=x.device)
+        return run_grouped_moe(x.to(torch.float16), w13, w2, s13, s2, z13, z2, ones, ids,
+                               out_dtype=torch.float32)
+
+    def _forward_generic(self, x, topk_ids, topk_weights, expert_fn=None, shared_fn=None):
+        """The exchange in plain torch ops: CPU ranks and custom experts (expert_fn), and the
+        prefill path on GPUs (expert_fn = the routed experts on received rows, shared_fn = the
+        shared expert on the rank's own tokens)."""
+        expert_fn = expert_fn or self.expert_fn
+        if expert_fn is None:
             raise RuntimeError("ExpertParallelMoE: CPU rows need an expert_fn (the built-in "
                                "experts run on CUDA weights)")
         T, H = x.shape
@@ -176,7 +215,7 @@ class ExpertParallelMoE:
         self._a2a(recv_x.view(W * T, H), send_x.view(W * T, H))
         dist.all_to_all_single(recv_id.view(W * T, k), send_id.view(W * T, k), group=self.group)
         dist.all_to_all_single(recv_w.view(W * T, k), send_w.view(W * T, k), group=self.group)
-        y = self.expert_fn(recv_x.view(W * T, H), recv_id.view(W * T, k), recv_w.view(W * T, k))
+        y = expert_fn(recv_x.view(W * T, H), recv_id.view(W * T, k), recv_w.view(W * T, k))
         y = y.to(torch.float32).contiguous()
         back = torch.empty_like(y)
         self._a2a(back, y)
@@ -186,8 +225,11 @@ class ExpertParallelMoE:
             sel = has[d]
             out[sel] = out[sel] + back[d, pos[d][sel]]
         if self.shared is not None:
-            ids = torch.zeros((T, 1), dtype=torch.int32, device=x.device)
-            out = out + self.expert_fn(x, ids, torch.ones((T, 1), device=x.device)).float()
+            if shared_fn is not None:
+                out = out + shared_fn(x).float()
+            else:
+                ids = torch.zeros((T, 1), dtype=torch.int32, device=x.device)
+                out = out + expert_fn(x, ids, torch.ones((T, 1), device=x.device)).float()
         self._finish_profile()
         return out
 
