@@ -800,9 +800,7 @@ decode_gemv_kernel(const DecArgs a, const __grid_constant__ CUtensorMap tmw) {
                     for (int v = 0; v < 4; ++v) tot[tg][v] = 0.f;
             }
             if (warp == 0 && lane == 0) DEC_TRACE(MODE, n_done, 3);
-#ifndef W4A8_DEC_SKIP_COMPUTE
             dec_compute(sm.st[st], r0, r1, ntg, PACKED || a.zeros != nullptr, tot);
-#endif
             __syncwarp();
             if (warp == 0 && lane == 0) DEC_TRACE(MODE, n_done, 2);
             __syncwarp();
@@ -814,10 +812,6 @@ decode_gemv_kernel(const DecArgs a, const __grid_constant__ CUtensorMap tmw) {
                 ph ^= 1;
             }
             if (!last) continue;
-#ifdef W4A8_DEC_SKIP_EPILOGUE
-            if (tot[0][0] == -12345.678f) a.meta[kMetaErr] = 7;  // keeps the MMAs alive
-            continue;
-#endif
             // ---- pass epilogue (warp-local: no barrier with the other warps) ----
             if (MODE == kGateUp) {
                 // SiLU rows (fp16) and their per-row amax for the down operand's scale
@@ -1330,11 +1324,7 @@ decode_tc_kernel(const DecArgs a) {
             TStage& S = sm.st[st];
             // token rows -> SW128 B tiles (16-byte unit u of row r at u ^ (r & 7)); the rows
             // from nrows on feed accumulator columns no one reads
-#ifdef W4A8_TC_NO_BCOPY  // experiment builds only: timing without the B tile copy
-            const int nb = 0;
-#else
             const int nb = sm.meta[st].nrows * (kDSpi * 8);
-#endif
             for (int i = threadIdx.x; i < nb; i += kTW * 32) {
                 const int r = i >> 5, v = i & 31, kb = v >> 3, uu = v & 7;
                 *reinterpret_cast<uint4*>(&S.bsw[kb][r * 128 + ((uu ^ (r & 7)) << 4)]) =
@@ -1358,13 +1348,8 @@ decode_tc_kernel(const DecArgs a) {
                     const uint4 qa = *reinterpret_cast<const uint4*>(wh + m * 128 + ((u0 ^ (m & 7)) << 4));
                     const uint32_t w[4] = {qa.x, qa.y, qa.z, qa.w};
                     uint32_t A[8];
-#ifdef W4A8_TC_NO_EXPAND  // experiment builds only: timing without the code expansion
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) A[2 * i] = A[2 * i + 1] = w[i];
-#else
 #pragma unroll
                     for (int i = 0; i < 4; ++i) codes8_to_e4m3_fma(w[i], a.one, a.m1, A[2 * i], A[2 * i + 1]);
-#endif
                     tmem_st8(tmem + lane_base + (ab * kTHalf + jj) * 32 + 8 * h, A);
                 }
                 if (warp == 0 && lane == 0 && k == 0) DEC_TRACE(MODE, n, 5);
@@ -1627,11 +1612,7 @@ int run_fused_decode(const DecInput& in, int64_t T, int64_t top_k, int64_t E,
     if (prep_smem > 48 * 1024)
         cudaFuncSetAttribute(decode_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)prep_smem);
-#ifdef W4A8_PREP_ALIGN_ONLY  // experiment builds only: time the routing sort alone
-    decode_prep_kernel<<<1, kPrepThreads, prep_smem, st>>>(a);
-#else
     decode_prep_kernel<<<(unsigned)(1 + (in.row_bytes ? 0 : T)), kPrepThreads, prep_smem, st>>>(a);
-#endif
     if (int rc = launch_status()) return rc;
     // 2. gate_up GEMV + SiLU (+ the down operand, by each expert's last unit)
     a.packed = static_cast<const uint8_t*>(p13);
@@ -1675,11 +1656,6 @@ int run_fused_decode(const DecInput& in, int64_t T, int64_t top_k, int64_t E,
 extern "C" W4A8_API int w4a8_debug_dec_trace(void* host, size_t bytes) {
     return (int)cudaMemcpyFromSymbol(host, w4a8::g_dec_trace, bytes);
 }
-#ifdef W4A8_WAIT_COUNT
-extern "C" W4A8_API int w4a8_debug_wait_iters(void* host) {
-    return (int)cudaMemcpyFromSymbol(host, w4a8::g_wait_iters, sizeof(w4a8::g_wait_iters));
-}
-#endif
 extern "C" W4A8_API int w4a8_debug_prep_trace(void* host) {
     return (int)cudaMemcpyFromSymbol(host, w4a8::g_prep_trace, sizeof(w4a8::g_prep_trace));
 }

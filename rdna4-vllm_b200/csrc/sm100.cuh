@@ -56,20 +56,11 @@ __device__ __forceinline__ bool mbar_try_sleep(uint64_t* bar, uint32_t parity, u
 
 // Bounded wait: a plain try_wait first, then suspending try_waits (up to 20 us each), giving up
 // after kWaitLimitNs; once any wait in the CTA has given up, later waits return at once.
-#ifdef W4A8_WAIT_COUNT  // experiment builds only: polling iterations per warp index
-__device__ unsigned long long g_wait_iters[2][32];
-#endif
 __device__ __forceinline__ void mbar_wait(uint64_t* bar, uint32_t parity, volatile int* bad) {
-#ifdef W4A8_WAIT_COUNT
-    atomicAdd(&g_wait_iters[0][(threadIdx.x >> 5) & 31], 1ull);
-#endif
     if (mbar_try(bar, parity)) return;
     if (*bad) return;
     const uint64_t t0 = global_ns();
     for (;;) {
-#ifdef W4A8_WAIT_COUNT
-        atomicAdd(&g_wait_iters[1][(threadIdx.x >> 5) & 31], 1ull);
-#endif
         if (mbar_try_sleep(bar, parity, 20000u)) return;
         if (*bad) return;
         if (global_ns() - t0 > kWaitLimitNs) {
