@@ -24,3 +24,16 @@ def test_reference_arm_prints_contract_line():
     cb = d["cpu_baseline"]
     assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["sample"]
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
+
+
+def test_stack_workload_reference_arm_is_unavailable():
+    """configs[4] (the expert-parallel stack) has no reference arm: the reference has no expert
+    parallelism. The arm prints the contract's `unavailable` line and exits 0."""
+    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--workload", "stack",
+                        "--steps", "1", "--warmup", "3"], cwd=ROOT, capture_output=True,
+                       text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1, r.stdout
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and "unavailable" in d
