@@ -178,3 +178,52 @@ def test_unequal_token_counts_raise_or_pad():
         assert err is None, err
         assert raised, f"rank {rank}: unequal T was accepted"
         assert ok, f"rank {rank}: max_tokens padding gave a wrong result"
+
+
+def _fake_grouped_moe(x, w1, w2, w1_s, w2_s, w1_zp, w2_zp, topk_weights, topk_ids,
+                      kernel="wmma", global_num_experts=None, expert_map=None,
+                      apply_router_weight_on_input=False, out_dtype=None):
+    """A stand-in for run_grouped_moe with the same id semantics: local expert e scales its
+    row by w1[e] (a scalar per expert here); ids that expert_map sends to -1 contribute
+    nothing."""
+    ids = topk_ids.long()
+    loc = expert_map.long()[ids] if expert_map is not None else ids
+    valid = loc >= 0
+    f = torch.where(valid, w1.float()[loc.clamp_min(0)], torch.zeros((), dtype=torch.float32))
+    y = (topk_weights.float() * f).sum(1, keepdim=True) * x.float()
+    return y.to(out_dtype or x.dtype)
+
+
+def _worker_prefill_map(rank, world, port, q):
+    try:
+        _init(rank, world, port)
+        import w4a8_fp8_wmma.moe_experts as me
+        me.run_grouped_moe = _fake_grouped_moe
+        torch.manual_seed(7 + rank)
+        T, H, E, k = 9, 16, 16, 4
+        E_loc = E // world
+        x = torch.randn(T, H).to(torch.float16)
+        ids = torch.stack([torch.randperm(E)[:k] for _ in range(T)]).to(torch.int32)
+        w = torch.rand(T, k)
+        # "weights": expert e (global) scales by 1 + e; the shared expert by 100
+        w1 = (1.0 + torch.arange(rank * E_loc, (rank + 1) * E_loc)).float()
+        shared = (torch.tensor([100.0]),) * 6
+        layer = ExpertParallelMoE(w1, w1, w1, w1, w1, w1, E, k, shared=shared)
+        out = layer._forward_generic(x, ids, w, layer._prefill_experts, layer._prefill_shared)
+        ref = ((w * (1.0 + ids.float())).sum(1, keepdim=True) + 100.0) * x.float()
+        q.put((rank, bool(torch.allclose(out, ref, rtol=1e-3, atol=1e-2)), None))
+    except Exception:  # noqa: BLE001
+        q.put((rank, False, traceback.format_exc()))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_prefill_path_maps_remote_slots_and_adds_shared(world):
+    """The GPU prefill path's exchange and id mapping on CPU ranks: each rank runs the
+    composition (a stand-in here) on received rows with slots owned elsewhere mapped to a
+    remote expert, and the shared expert on its own tokens."""
+    res = _spawn(_worker_prefill_map, world)
+    for r, ok, err in res:
+        assert ok, err
