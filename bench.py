@@ -68,7 +68,9 @@ def base_config(workload: str, world: int, layers: int = 1) -> dict:
             "shared_experts": 1, "top_k": TOP_K, "group": GROUP, "layers": layers,
             "routing": "softmax top-8 renormalised" + (" + Zipf(1.1) expert bias"
                                                        if cfg["zipf"] else ""),
-            "parallelism": f"ep{world}" if world > 1 else "single"}
+            "parallelism": f"ep{world}" if world > 1 else "single",
+            "l2": ("touched weights > 126 MB L2 (no flush)" if world == 1 else
+                   "per-rank weights ~53-105 MB; inputs re-read each step")}
 
 
 def host_info() -> dict:
@@ -273,15 +275,14 @@ def run_ours(args):
     ep = ep_report(torch, dist, world, rank, dev, layer, x, ids, tw, wts, shared) if world > 1 else None
     if rank != 0:
         _leave(dist, world)
+    # config is the workload description both arms print, identical between them
     config = base_config(args.workload, world)
-    config.update({
-        "l2": "touched weights > 126 MB L2 (no flush)" if world == 1 else
-              "per-rank weights ~53-105 MB; inputs re-read each step",
+    layer_info = {
         "rank0_hbm_bytes_per_step": layer_bytes,
         "layer_hbm_gbs": round(layer_bytes / (ms / 1e3) / 1e9, 1),
         "layer_hbm_frac_of_measured": round(layer_bytes / (ms / 1e3) / 1e9 / hbm, 4),
         "layer_tflops": round(flops / (ms / 1e3) / 1e12, 2),
-        "graph": "one CUDA graph per step" if graph is not None else "eager steps"})
+        "graph": "one CUDA graph per step" if graph is not None else "eager steps"}
     res = {
         "metric": metric_name(args.workload),
         "value": round(tokens_per_s, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -289,6 +290,7 @@ def run_ours(args):
         "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 x int4 -> fp32 (fp16 io)",
         "data": "synthetic (seeded; random-init weights of the layer's shapes)",
         "config": config,
+        "layer": layer_info,
         "roofline": dom,
         "clocks": clk.summary(),
         "e2e": e2e,
